@@ -1,0 +1,432 @@
+#!/usr/bin/env python
+"""bench.py — weight-only quantized GEMV throughput on B200.
+
+Workload (the configuration the metric is quoted
+on): W4A16 group-128 GEMV / skinny GEMM, x fp16 [M, K] ~ N(0,1) with M in
+{1, 8, 32}, (K, N) in {(1536, 8960), (8960, 1536)}, W ~ N(0, 0.02) quantized
+by the reference's RTN quantizer into the reference's packed format.
+
+One step = every (M, shape) pair over COPIES distinct weight copies per shape
+(24 x 2 x 7.1 MB = 341 MB, 2.7x the 126 MB L2, cycled so no launch finds its
+weights in L2), i.e. 144 kernel launches, recorded once into a CUDA graph.
+
+  value   = algorithmic bytes of all ranks / device time of K steps (GB/s);
+            algorithmic bytes per launch = N*K/2 + 2*N*K/128 + 2*M*K + 2*M*N.
+  e2e     = the same, through the public API with host buffers: each step
+            copies its activations from pinned host memory and every output
+            back to pinned host memory inside the timed region.
+  roofline: the GEMV kernel's achieved GB/s against the measured HBM copy
+            bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline: the reference's CPU path (dequantize to fp32, then an fp32
+            linear; restated in oracle/) on the host cores, bounded sample.
+
+`--impl reference` times that CPU path alone (rank 0), on the same
+metric/config.  Multi-GPU (torchrun): every rank runs the same workload on
+its own weight copies (weak scaling, no data-path collective); the device
+time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "llm-inference-optimizer_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "W4A16/W8A16 decode GEMV HBM GB/s (% of 8 TB/s); prefill GEMM TFLOPS"
+MS = (1, 8, 32)
+SHAPES = ((1536, 8960), (8960, 1536))      # (K, N)
+COPIES = 24
+WORKLOAD = ("config1: W4A16 group-128 GEMV, M in {1,8,32}, (K,N) in {(1536,8960),(8960,1536)}, "
+            "reference split-half int4 format, fp16 scales [K/128,N], no bias, "
+            f"{COPIES} weight copies per shape cycled (341 MB > L2)")
+
+
+def algo_bytes(M: int, K: int, N: int) -> int:
+    """Algorithmic bytes of one W4A16 launch: packed weights + fp16 scales +
+    fp16 activations in + fp16 outputs out."""
+    return N * K // 2 + 2 * N * (K // 128) + 2 * M * K + 2 * M * N
+
+
+def step_bytes() -> int:
+    return sum(algo_bytes(M, K, N) * COPIES for M in MS for K, N in SHAPES)
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary
+    (profiles/traffic.txt, lines 'name: bytes_per_launch'), else None."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if ":" in line and not line.lstrip().startswith("#"):
+            k, v = line.split(":", 1)
+            if k.strip() == kernel:
+                try:
+                    return float(v.split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML during the timed
+    regions (read-only; no setting is changed)."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, torch_dev: int):
+        self.samples = []
+        self.active = False
+        self.stop_ev = threading.Event()
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_dev)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+        except Exception:
+            self.handle = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _reasons(self):
+        n = self.nvml
+        for fn in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            if hasattr(n, fn):
+                return getattr(n, fn)(self.handle)
+        return 0
+
+    def _run(self):
+        while not self.stop_ev.is_set():
+            if self.active and self.handle is not None:
+                try:
+                    mhz = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                    self.samples.append((mhz, int(self._reasons())))
+                except Exception:
+                    pass
+            time.sleep(0.02)
+
+    def start(self):
+        self.thread.start()
+
+    def stop(self):
+        self.stop_ev.set()
+        self.thread.join(timeout=2)
+
+    def summary(self):
+        if self.handle is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = set()
+        for _, r in self.samples:
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_reference_run(host_layers, host_x, *, seconds=None, steps=None, warmup=0):
+    """Times the reference's CPU path (oracle restatement of
+    w4a16_reference: dequantize to fp32, fp32 linear) over the config-1
+    (M, shape) pairs, cycling pairs; rows are split over all host cores
+    (numpy releases the GIL).  Returns (GB/s, seconds, bytes, launches, cores)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    from oracle import qlinear_oracle as orc
+
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(1)
+    except Exception:
+        limiter = None
+    pool = ThreadPoolExecutor(cores)
+    combos = [(M, K, N) for M in MS for K, N in SHAPES]
+
+    def one(M, K, N):
+        packed, scales = host_layers[(K, N)]
+        x = host_x[(M, K)]
+        edges = np.linspace(0, N, cores + 1).astype(int)
+        futs = [pool.submit(orc.w4a16_reference_f32, x, packed[a:b], scales[:, a:b])
+                for a, b in zip(edges[:-1], edges[1:]) if b > a]
+        return np.concatenate([f.result() for f in futs], axis=1)
+
+    for i in range(warmup):
+        one(*combos[i % len(combos)])
+    nbytes = 0
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        M, K, N = combos[n % len(combos)]
+        one(M, K, N)
+        nbytes += algo_bytes(M, K, N)
+        n += 1
+        el = time.perf_counter() - t0
+        if steps is not None and n >= steps:
+            break
+        if seconds is not None and el >= seconds:
+            break
+    el = time.perf_counter() - t0
+    pool.shutdown()
+    if limiter is not None:
+        limiter.unregister() if hasattr(limiter, "unregister") else None
+    return nbytes / el / 1e9, el, nbytes, n, cores
+
+
+def host_workload(seed=0):
+    """Config-1 weights/activations on the host (numpy), for the CPU legs."""
+    import numpy as np
+    from oracle import qlinear_oracle as orc
+    rng = np.random.default_rng(seed)
+    layers = {}
+    for K, N in SHAPES:
+        w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float16)
+        layers[(K, N)] = orc.quantize_int4_groups(w)
+    xs = {(M, K): rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+          for M in MS for K, _ in SHAPES}
+    return layers, xs
+
+
+# ------------------------------------------------------------------- arms
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    layers, xs = host_workload()
+    gbs, el, nbytes, n, cores = cpu_reference_run(layers, xs, steps=args.steps, warmup=args.warmup)
+    line = {
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / max(n, 1) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": WORKLOAD,
+                   "step": "one (M, shape) GEMV of config 1, cycling the six pairs"},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} GEMVs (config-1 pairs cycled), {nbytes / 1e6:.1f} MB algorithmic"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from qlinear.kernels.w4a16_matmul import w4a16_linear, w4a16_quantize_cuda
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    # weights: COPIES distinct copies per shape, quantized on the device
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    layers = {}
+    for K, N in SHAPES:
+        copies = []
+        for _ in range(COPIES):
+            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+            copies.append(w4a16_quantize_cuda(w))
+            del w
+        layers[(K, N)] = copies
+    xs = {(M, K): torch.randn(M, K, generator=gen, device=dev).half() for M in MS for K, _ in SHAPES}
+    # one output buffer; every launch writes its own slice
+    slots = []
+    off = 0
+    for M in MS:
+        for K, N in SHAPES:
+            for c in range(COPIES):
+                slots.append((M, K, N, c, off))
+                off += M * N
+    ybuf = torch.empty(off, dtype=torch.float16, device=dev)
+
+    def step():
+        for M, K, N, c, o in slots:
+            packed, scales = layers[(K, N)][c]
+            w4a16_linear(xs[(M, K)], packed, scales, out=ybuf[o:o + M * N].view(M, N))
+
+    launches_per_step = len(slots)
+    nbytes = step_bytes()
+
+    # eager warm-up (sizes the split-K workspace), then capture
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize(dev)
+        g_val = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_val, stream=stream):
+            step()
+        # e2e: pinned host activations in, every output back to pinned host
+        x_host = {k: v.cpu().pin_memory() for k, v in xs.items()}
+        y_host = torch.empty(ybuf.shape, dtype=ybuf.dtype, pin_memory=True)
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e, stream=stream):
+            for k, v in xs.items():
+                v.copy_(x_host[k], non_blocking=True)
+            step()
+            y_host.copy_(ybuf, non_blocking=True)
+    h2d = sum(v.numel() * 2 for v in xs.values())
+    d2h = ybuf.numel() * 2
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+
+    def timed(graph, K, W):
+        with torch.cuda.stream(stream):
+            for _ in range(W):
+                graph.replay()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            clocks.active = True
+            e0.record(stream)
+            for _ in range(K):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            clocks.active = False
+            if world > 1:
+                dist.barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms_val = timed(g_val, args.steps, args.warmup)
+    ms_e2e = timed(g_e2e, args.steps, args.warmup)
+
+    # per-(M, shape) breakdown on this rank (same cycling, graphs of COPIES launches)
+    detail = {}
+    reps = max(20, args.steps // 4)
+    with torch.cuda.stream(stream):
+        for M in MS:
+            for K, N in SHAPES:
+                sub = [s for s in slots if s[0] == M and s[1] == K]
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for _, K_, N_, c, o in sub:
+                        packed, scales = layers[(K_, N_)][c]
+                        w4a16_linear(xs[(M, K_)], packed, scales, out=ybuf[o:o + M * N_].view(M, N_))
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize(dev)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                clocks.active = True
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                clocks.active = False
+                us = e0.elapsed_time(e1) * 1e3 / (reps * len(sub))
+                gbs = algo_bytes(M, K, N) / (us * 1e-6) / 1e9
+                detail[f"M{M}_K{K}_N{N}"] = {"us_per_launch": round(us, 3), "GBps": round(gbs, 1)}
+                del g
+    clocks.stop()
+
+    peak, peak_kind = measured_peaks()
+    per_rank_gbs = nbytes / (ms_val / args.steps * 1e-3) / 1e9
+    value = world * per_rank_gbs
+    e2e_gbs = world * nbytes / (ms_e2e / args.steps * 1e-3) / 1e9
+    avg_launch_bytes = nbytes / launches_per_step
+    traffic = profiled_traffic("qgemv_w4_config1")
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        hl = {(K, N): (layers[(K, N)][0][0].cpu().numpy(), layers[(K, N)][0][1].cpu().numpy())
+              for K, N in SHAPES}
+        hx = {k: v.cpu().numpy() for k, v in xs.items()}
+        gbs, el, cb, n, cores = cpu_reference_run(hl, hx, seconds=args.cpu_seconds, warmup=2)
+        cpu_baseline = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                        "sample": f"{n} config-1 GEMVs ({el:.1f} s, {cb / 1e6:.0f} MB algorithmic), "
+                                  "oracle restatement of the reference's dequantize-then-fp32-linear"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_val / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": list(MS), "l2": "inputs larger than L2 "
+                       "(weights cycled; each launch's weights last touched 47 launches earlier)",
+                       "launches_per_step": launches_per_step, "bytes_per_step": nbytes,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": per_rank_gbs / peak, "peak_kind": peak_kind,
+                         "kernel": "qgemv_kernel<4,0,*> (W4A16 decode GEMV)",
+                         "bytes_per_launch": avg_launch_bytes,
+                         "traffic": traffic, "pct_of_8TBs": per_rank_gbs / 8000.0},
+            "cpu_baseline": cpu_baseline,
+            "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e / args.steps,
+                    "path": "QuantizedLinearInt4 API (w4a16_linear) in a CUDA graph with pinned host I/O"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+            "detail": detail,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del g_val, g_e2e
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

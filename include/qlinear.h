@@ -1,0 +1,168 @@
+/*
+ * qlinear.h — C ABI of libqlinear.so, the B200 (sm_100a) weight-only
+ * quantized linear layer (W8A16 and W4A16, group 128).
+ *
+ * This is the drop-in boundary for the quantized-linear path of
+ * SriramL1/LLM-inference-optimizer.  Each entry point replaces one function
+ * of the reference (paths relative to the reference repository root):
+ *
+ *   ql_w8a16_linear        <- w8a16_linear          src/kernels/w8a16_matmul_triton.py:102-134
+ *                             (kernel _w8a16_matmul_kernel, :39-86)
+ *   ql_w4a16_linear        <- w4a16_linear          src/kernels/w4a16_matmul_triton.py:134-170
+ *                             (kernel _w4a16_matmul_kernel, :62-117)
+ *   ql_w8a16_dequantize    <- QuantizedLinearInt8.dequantized_weight  src/quantization/int8.py:52-53
+ *   ql_w4a16_dequantize    <- dequantize_int4       src/kernels/w4a16_matmul_triton.py:173-178
+ *   ql_w4a16_unpack        <- unpack_int4           src/kernels/w4a16_matmul_triton.py:52-58
+ *   ql_w8a16_quantize      <- QuantizedLinearInt8.from_linear  src/quantization/int8.py:44-50
+ *   ql_w4a16_quantize      <- QuantizedLinearInt4.from_linear  src/quantization/int4.py:37-49
+ *                             (+ pack_int4, w4a16_matmul_triton.py:42-49)
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  All pointers are device pointers on the
+ *     current CUDA device unless stated otherwise; `stream` is a cudaStream_t
+ *     (NULL = legacy default stream).  Every call is asynchronous on `stream`,
+ *     allocates nothing, never synchronises the device, and is safe to record
+ *     into a CUDA graph (no host-side sync, no lazy compilation).
+ *   - Matrices are row-major with the leading dimension given in ELEMENTS
+ *     (bytes for packed int4 rows).  The reduction dimension K is contiguous.
+ *   - Every function returns a status (QL_OK = 0, negative on error) and never
+ *     aborts; ql_strerror() turns a status into a message.  Argument errors
+ *     are detected on the host before anything is launched.
+ *   - The reference's Python asserts (w8a16_matmul_triton.py:110-113,
+ *     w4a16_matmul_triton.py:142-148) stay in the Python wrapper; this layer
+ *     re-checks what it needs for memory safety.
+ */
+#ifndef QLINEAR_H_
+#define QLINEAR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- status */
+#define QL_OK                   0
+#define QL_ERR_NULL_POINTER    -1   /* a required pointer is NULL                       */
+#define QL_ERR_BAD_SHAPE       -2   /* negative size, K % 128 != 0 for int4, ...          */
+#define QL_ERR_BAD_STRIDE      -3   /* leading dimension smaller than the row            */
+#define QL_ERR_UNSUPPORTED     -4   /* dtype / layout / flag this build does not handle  */
+#define QL_ERR_WORKSPACE       -5   /* workspace too small for the requested plan        */
+#define QL_ERR_CUDA            -6   /* a CUDA runtime call failed (launch, attribute)    */
+#define QL_ERR_DEVICE          -7   /* no usable sm_100 device / driver entry point      */
+#define QL_ERR_DEVICE_TIMEOUT  -8   /* a kernel gave up a bounded wait (see below)       */
+
+/* ------------------------------------------------------------------ dtypes */
+#define QL_DTYPE_F16   0
+#define QL_DTYPE_F32   1
+#define QL_DTYPE_BF16  2
+
+/* ---------------------------------------------------- int4 packing layouts */
+/* The reference's layout: inside each group of 128 along K, byte j (0..63)
+ * holds element j in the low nibble and element j+64 in the high nibble
+ * (w4a16_matmul_triton.py:10-20, 42-49).  Nibbles are offset-binary q+8.  */
+#define QL_W4_LAYOUT_SPLIT_HALF  0
+/* Adjacent pairs: byte i holds k = 2i (low nibble) and k = 2i+1 (high).   */
+#define QL_W4_LAYOUT_ADJACENT    1
+
+/* ------------------------------------------------------------------- flags */
+/* Launch with programmatic dependent launch: the kernel starts streaming its
+ * weights (and int4 scales) before the preceding kernel in the stream has
+ * finished, and waits for it only before reading x / writing out / using the
+ * workspace.  Valid whenever the weight and scale buffers are not written by
+ * the kernels queued just before this call (true for inference).           */
+#define QL_FLAG_PDL             0x1u
+/* Force the tensor-core GEMM (prefill) path regardless of M.  Test hook.   */
+#define QL_FLAG_FORCE_GEMM      0x2u
+/* Force the decode (GEMV / skinny) path regardless of M.  Test hook.        */
+#define QL_FLAG_FORCE_GEMV      0x4u
+/* Force the portable CUDA-core path (any shape / alignment).  Test hook.    */
+#define QL_FLAG_FORCE_GENERIC   0x8u
+
+/* ------------------------------------------------------------------ linear */
+/*
+ * out[M, N] = x[M, K] @ (w_q[N, K] * scale[N])^T (+ bias[N]),
+ * fp32 accumulation, fp16 output (the dtype of x).
+ *   x        fp16 [M, ldx]           (x_dtype must be QL_DTYPE_F16)
+ *   w_q      int8 [N, ldw]
+ *   scale    [N], scale_dtype QL_DTYPE_F32 (reference) or QL_DTYPE_F16
+ *   bias     [N] or NULL, bias_dtype QL_DTYPE_F16 or QL_DTYPE_F32
+ *   out      fp16 [M, ldo]
+ *   workspace / workspace_bytes: optional scratch for split-K.  Must be
+ *     zero-filled before its first use; every call leaves it zero-filled.
+ *     With NULL (or too small) the kernel is planned without split-K, which
+ *     is always valid but can be slower for tall-K shapes.  Calls that share
+ *     one workspace must not run concurrently (use one per stream).
+ */
+int ql_w8a16_linear(const void* x, int x_dtype,
+                    const void* w_q,
+                    const void* scale, int scale_dtype,
+                    const void* bias, int bias_dtype,
+                    void* out,
+                    int64_t M, int64_t N, int64_t K,
+                    int64_t ldx, int64_t ldw, int64_t ldo,
+                    void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream);
+
+/*
+ * out[M, N] = x[M, K] @ dequant(w_packed, scales)^T (+ bias[N]),
+ * dequant = (nibble - 8) * scales[k / 128, n], fp32 accumulation.
+ *   w_packed uint8 [N, ldw] (ldw in bytes, >= K/2), layout as above
+ *   scales   fp16 [K/128, lds]  (lds >= N)
+ *   K must be a multiple of 128.
+ */
+int ql_w4a16_linear(const void* x, int x_dtype,
+                    const void* w_packed, int layout,
+                    const void* scales,
+                    const void* bias, int bias_dtype,
+                    void* out,
+                    int64_t M, int64_t N, int64_t K,
+                    int64_t ldx, int64_t ldw, int64_t lds, int64_t ldo,
+                    void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream);
+
+/* Workspace bytes the fastest plan for (M, N, K) needs on the current device
+ * (0 when that plan needs none).  Deterministic for a given device. */
+size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
+size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* -------------------------------------------------------- format helpers */
+/* out_f32[N, K] = w_q * scale (fp32), bit-exact with the reference. */
+int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype,
+                        float* out, int64_t N, int64_t K, int64_t ldw,
+                        void* stream);
+/* out_f32[N, K] = (nibble - 8) * scales (fp32), bit-exact with the reference.
+ * Uses the same register-level nibble decoder as the GEMV/GEMM kernels. */
+int ql_w4a16_dequantize(const void* w_packed, int layout, const void* scales,
+                        float* out, int64_t N, int64_t K, int64_t ldw, int64_t lds,
+                        void* stream);
+/* out_u8[N, K] = the raw nibbles (0..15) in logical k order. */
+int ql_w4a16_unpack(const void* w_packed, int layout, uint8_t* out,
+                    int64_t N, int64_t K, int64_t ldw, void* stream);
+
+/* On-device quantizers, bit-exact with the reference's from_linear.
+ *   ql_w8a16_quantize: w fp16 [N, K] -> w_q int8 [N, K], scale fp32 [N]
+ *   ql_w4a16_quantize: w fp16 [N, K] -> packed uint8 [N, K/2] (layout),
+ *                      scales fp16 [K/128, N]; q clamped to [qmin, 7]
+ *                      (reference: qmin = -7). */
+int ql_w8a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
+                      int8_t* w_q, float* scale, void* stream);
+int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
+                      int qmin, int layout, uint8_t* w_packed, void* scales,
+                      void* stream);
+
+/* ------------------------------------------------------------- diagnostics */
+const char* ql_strerror(int status);
+/* Version as (major << 16) | (minor << 8) | patch. */
+int ql_version(void);
+/* Kernels never trap: a bounded wait that runs out records a code in a
+ * device-global word and the kernel returns early.  These read (and clear)
+ * that word on the current device; they synchronise the device. */
+int ql_device_error(int* code_out);
+int ql_clear_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QLINEAR_H_ */

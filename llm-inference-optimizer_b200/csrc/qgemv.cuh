@@ -1,0 +1,383 @@
+// qgemv.cuh — decode-shaped (small M) dequant-fused GEMV / skinny GEMM.
+//
+// Replaces the reference's Triton kernels for small M
+// (_w8a16_matmul_kernel, src/kernels/w8a16_matmul_triton.py:39-86;
+//  _w4a16_matmul_kernel, src/kernels/w4a16_matmul_triton.py:62-117).
+//
+// Work decomposition
+//   * A "tile" is 16 consecutive weight rows (output columns n).  A CTA owns
+//     `tpc` consecutive tiles and one K-split of `kb_per_split` k-blocks; a
+//     k-block is 128 bytes of every row (256 k for int4, 128 k for int8).
+//   * One producer thread streams the CTA's weight slice through a ring of
+//     `stages` shared-memory slots with 2-D TMA (box = tpc*16 rows x 128 B,
+//     128-byte swizzle), completion on mbarriers.  With programmatic
+//     dependent launch the whole prologue of that stream is issued before
+//     the kernel waits for its predecessor: weights do not depend on it.
+//   * Consumer warps: `wpt` warps per tile, each taking every wpt-th k-block.
+//     A warp reads two 16-byte chunks per 64-byte k-step (rows g and g+8 of
+//     its tile), decodes them in registers to exact fp16 integers, and
+//     issues mma.sync m16n8k16 with the weights as the 16-row A operand and
+//     the activations (x slice staged in shared memory) as the n8 operand
+//     ("swap-AB": the batch is the narrow side).  fp32 accumulation; the
+//     int4 group scale is applied to each 128-k group partial in fp32, the
+//     int8 row scale once at the end — as in the reference kernels.
+//   * Warps of a tile reduce through shared memory in a fixed order.  With
+//     more than one K-split, each CTA writes an fp32 partial to its own
+//     workspace slot and the last CTA to arrive (atomic counter) sums the
+//     slots in slot order, applies scale/bias and resets the counter, so the
+//     result is deterministic and the workspace stays zeroed.
+#pragma once
+
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gemv {
+
+constexpr int kTileRows = 16;
+constexpr int kBlockBytes = 128;    // k-block width = TMA box inner extent (SW128)
+constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxThreads = (kMaxConsumerWarps + 1) * 32;
+
+struct Params {
+  const __half* x;        // [M, ldx]
+  const void* scale;      // int8: [N] (f32 or f16); int4: [K/128, lds] f16
+  const void* bias;       // [N] or nullptr
+  __half* out;            // [M, ldo]
+  long long ldx, lds, ldo;
+  int M, N, K;
+  int kbytes;             // valid bytes of one weight row: K/2 (int4) or K (int8)
+  int nkb;                // ceil(kbytes / 128)
+  int kb_per_split;
+  int ks;                 // number of K-splits (gridDim.y)
+  int tpc;                // tiles per CTA
+  int wpt;                // consumer warps per tile
+  int stages;             // ring depth
+  int x_stride;           // halves per staged x row
+  int x_rows;             // staged x rows = min(8*MT, M)
+  int scale_f32;          // int8 scale dtype
+  int bias_f32;           // bias dtype
+  int early_weights;      // stream weights before griddepcontrol.wait
+  uint32_t* counters;     // [gridDim.z * gridDim.x] (ks > 1)
+  float* partials;        // [gridDim.z][gridDim.x][ks][mc][tpc*16] (ks > 1)
+  unsigned* err;          // device error word
+};
+
+// Shared-memory carve-up, identical on host and device.
+struct Smem {
+  size_t ring, red, region0, x, sc, bars, total;
+};
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+__host__ __device__ inline Smem smem_layout(int wbits, int mc, int x_rows, int tpc, int wpt,
+                                            int stages, int x_stride, int kb_per_split) {
+  Smem s;
+  s.ring = (size_t)stages * tpc * kTileRows * kBlockBytes;
+  s.red = (size_t)tpc * wpt * kTileRows * mc * 4;
+  s.region0 = align_up(s.ring > s.red ? s.ring : s.red, 1024);
+  s.x = align_up((size_t)x_rows * x_stride * 2, 16);
+  s.sc = wbits == 4 ? align_up((size_t)kb_per_split * 2 * tpc * kTileRows * 4, 16) : 0;
+  s.bars = align_up((size_t)2 * stages * 8 + 16, 16);
+  s.total = 1024 /* base alignment slack */ + s.region0 + s.x + s.sc + s.bars;
+  return s;
+}
+
+template <int WBITS>
+__device__ __forceinline__ float finish_value(const Params& p, float v, int n) {
+  if (WBITS == 8) {
+    const float s = p.scale_f32 ? static_cast<const float*>(p.scale)[n]
+                                : __half2float(static_cast<const __half*>(p.scale)[n]);
+    v *= s;
+  }
+  if (p.bias) {
+    v += p.bias_f32 ? static_cast<const float*>(p.bias)[n]
+                    : __half2float(static_cast<const __half*>(p.bias)[n]);
+  }
+  return v;
+}
+
+// MT = number of n8 batch tiles per CTA (mc = 8*MT batch rows per grid.z slice).
+template <int WBITS, int LAYOUT, int MT>
+__global__ void __launch_bounds__(kMaxThreads, 1)
+    qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+  constexpr int MC = 8 * MT;
+  constexpr int EPK = WBITS == 4 ? 256 : 128;      // k elements per k-block
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte-swizzled TMA destinations need 1024-byte aligned shared addresses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+
+  const int tpc = p.tpc, wpt = p.wpt, stages = p.stages;
+  const int ncw = tpc * wpt;                 // consumer warps
+  const int nct = ncw * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_cta = tpc * kTileRows;
+  const uint32_t box_bytes = static_cast<uint32_t>(rows_cta * kBlockBytes);
+
+  const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, p.x_stride, p.kb_per_split);
+  uint8_t* ring = smem;
+  __half* xs = reinterpret_cast<__half*>(smem + L.region0);
+  float* ssc = reinterpret_cast<float*>(smem + L.region0 + L.x);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.region0 + L.x + L.sc);
+  uint64_t* empty = full + stages;
+  int* last_flag = reinterpret_cast<int*>(empty + stages);
+
+  const int blk = blockIdx.x, split = blockIdx.y, mchunk = blockIdx.z;
+  const int row0 = blk * rows_cta;
+  const int kb0 = split * p.kb_per_split;
+  const int kbc = min(p.kb_per_split, p.nkb - kb0);
+  const int m0 = mchunk * MC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, tpc);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer
+  if (warp == ncw) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap_w);
+      const uint64_t pol = l2_policy_evict_first();
+      if (!p.early_weights) griddep_wait();
+      const int npre = min(stages, kbc);
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive_expect_tx(full + i, box_bytes);
+        tma_load_2d(smem_u32(ring + (size_t)i * box_bytes), &tmap_w, (kb0 + i) * kBlockBytes, row0,
+                    full + i, pol);
+      }
+      for (int i = stages; i < kbc; ++i) {
+        const int s = i % stages;
+        const uint32_t par = ((i / stages) - 1) & 1;
+        mbar_wait(empty + s, par, p.err, kDevErrEmptyWait);   // on timeout: error recorded, go on
+        mbar_arrive_expect_tx(full + s, box_bytes);
+        tma_load_2d(smem_u32(ring + (size_t)s * box_bytes), &tmap_w, (kb0 + i) * kBlockBytes, row0,
+                    full + s, pol);
+      }
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------- consumers
+  const int ctid = threadIdx.x;
+  const int tt = warp / wpt, w = warp % wpt;
+  const int g = lane >> 2, c = lane & 3;
+
+  // int4 group scales of this CTA's rows and groups -> fp32 in shared
+  // memory.  Scales are static like the weights, so this runs before the
+  // dependency wait.
+  if (WBITS == 4) {
+    const int G = p.K / 128;
+    const int g0 = kb0 * 2;
+    const int ng = min(kbc * 2, G - g0);
+    const __half* sc = static_cast<const __half*>(p.scale);
+    for (int idx = ctid; idx < ng * rows_cta; idx += nct) {
+      const int gl = idx / rows_cta, r = idx - gl * rows_cta;
+      const int n = row0 + r;
+      ssc[idx] = n < p.N ? __half2float(sc[(long long)(g0 + gl) * p.lds + n]) : 0.f;
+    }
+  }
+
+  griddep_wait();   // x (and out / workspace) may belong to the previous kernel
+
+  const int mvalid = min(MC, p.M - m0);
+  // x slice [m0, m0+mvalid) x [kx0, kx0 + kbc*EPK) -> shared memory; k past
+  // K reads as zero.  Rows >= mvalid are never read.
+  {
+    const int kx0 = kb0 * EPK;
+    const int nvec = kbc * EPK / 8;
+    for (int idx = ctid; idx < mvalid * nvec; idx += nct) {
+      const int mr = idx / nvec, v = idx - mr * nvec;
+      const int k = kx0 + v * 8;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (k < p.K) val = ldg_cg_v4(p.x + (long long)(m0 + mr) * p.ldx + k);
+      *reinterpret_cast<uint4*>(xs + mr * p.x_stride + v * 8) = val;
+    }
+  }
+  named_bar_sync(1, nct);
+  griddep_launch_dependents();
+
+  float acc[MT][4];
+  #pragma unroll
+  for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+
+  // mma row g <-> tile row prow: keeps the two rows a quarter-warp reads in
+  // different 16-byte bank groups of the swizzled stage.
+  const int prow = (g >> 1) | ((g & 1) << 2);
+  const int rA = tt * kTileRows + prow, rB = rA + 8;
+  const uint32_t ring_s = smem_u32(ring);
+  const uint32_t xs_s = smem_u32(xs);
+  const int valid_bytes = p.kbytes - kb0 * kBlockBytes;
+
+  for (int i = w; i < kbc; i += wpt) {
+    const int s = i % stages;
+    const bool ok = mbar_wait(full + s, (i / stages) & 1, p.err, kDevErrFullWait);
+    if (ok) {
+      const uint32_t stage_s = ring_s + (uint32_t)s * box_bytes;
+      #pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int byte_off = i * kBlockBytes + h * 64;
+        if (byte_off >= valid_bytes) break;
+        const int q = h * 4 + c;
+        const uint4 wa = lds128(stage_s + rA * kBlockBytes + ((q ^ (rA & 7)) << 4));
+        const uint4 wb = lds128(stage_s + rB * kBlockBytes + ((q ^ (rB & 7)) << 4));
+        const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
+        const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
+        if (WBITS == 4) {
+          const int gl = i * 2 + h;                 // group index within the split
+          const int kg = gl * 128;                  // its first k (relative to kx0)
+          // Activation offsets of the two 16-element runs this lane needs:
+          // split-half: low nibbles k = kg+16c.., high nibbles k = kg+64+16c..
+          // adjacent:   k = kg+32c .. kg+32c+31
+          const int e0 = LAYOUT == 0 ? kg + 16 * c : kg + 32 * c;
+          const int e1 = LAYOUT == 0 ? kg + 64 + 16 * c : kg + 32 * c + 16;
+          uint32_t bx0[MT][8], bx1[MT][8];
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
+            if (t * 8 + g < mvalid) {
+              const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * p.x_stride) * 2u;
+              v0 = lds128(xr + e0 * 2);
+              v1 = lds128(xr + e0 * 2 + 16);
+              v2 = lds128(xr + e1 * 2);
+              v3 = lds128(xr + e1 * 2 + 16);
+            }
+            bx0[t][0] = v0.x; bx0[t][1] = v0.y; bx0[t][2] = v0.z; bx0[t][3] = v0.w;
+            bx0[t][4] = v1.x; bx0[t][5] = v1.y; bx0[t][6] = v1.z; bx0[t][7] = v1.w;
+            bx1[t][0] = v2.x; bx1[t][1] = v2.y; bx1[t][2] = v2.z; bx1[t][3] = v2.w;
+            bx1[t][4] = v3.x; bx1[t][5] = v3.y; bx1[t][6] = v3.z; bx1[t][7] = v3.w;
+          }
+          float part[MT][4];
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) part[t][0] = part[t][1] = part[t][2] = part[t][3] = 0.f;
+          #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (LAYOUT == 0) {
+              uint32_t al01, al23, ah01, ah23, bl01, bl23, bh01, bh23;
+              dec_w4_split(wA[j], al01, al23, ah01, ah23);
+              dec_w4_split(wB[j], bl01, bl23, bh01, bh23);
+              #pragma unroll
+              for (int t = 0; t < MT; ++t) {
+                // low nibbles: k = kg + 16c + 4j + {0..3}
+                mma_16816(part[t], al01, bl01, al23, bl23, bx0[t][2 * j], bx0[t][2 * j + 1]);
+                // high nibbles: k = kg + 64 + 16c + 4j + {0..3}
+                mma_16816(part[t], ah01, bh01, ah23, bh23, bx1[t][2 * j], bx1[t][2 * j + 1]);
+              }
+            } else {
+              uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
+              dec_w4_adjacent(wA[j], a01, a23, a45, a67);
+              dec_w4_adjacent(wB[j], b01, b23, b45, b67);
+              const int jj = (j & 1) * 4;
+              #pragma unroll
+              for (int t = 0; t < MT; ++t) {
+                // k = kg + 32c + 8j + {0..7}
+                const uint32_t* bx = j < 2 ? bx0[t] : bx1[t];
+                mma_16816(part[t], a01, b01, a23, b23, bx[jj], bx[jj + 1]);
+                mma_16816(part[t], a45, b45, a67, b67, bx[jj + 2], bx[jj + 3]);
+              }
+            }
+          }
+          const float sA = ssc[gl * rows_cta + rA];
+          const float sB = ssc[gl * rows_cta + rB];
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            acc[t][0] = fmaf(part[t][0], sA, acc[t][0]);
+            acc[t][1] = fmaf(part[t][1], sA, acc[t][1]);
+            acc[t][2] = fmaf(part[t][2], sB, acc[t][2]);
+            acc[t][3] = fmaf(part[t][3], sB, acc[t][3]);
+          }
+        } else {
+          // int8: k = byte_off + 16c + 4j + {0..3}
+          const int e0 = byte_off + 16 * c;
+          uint32_t bx[MT][8];
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+            if (t * 8 + g < mvalid) {
+              const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * p.x_stride) * 2u;
+              v0 = lds128(xr + e0 * 2);
+              v1 = lds128(xr + e0 * 2 + 16);
+            }
+            bx[t][0] = v0.x; bx[t][1] = v0.y; bx[t][2] = v0.z; bx[t][3] = v0.w;
+            bx[t][4] = v1.x; bx[t][5] = v1.y; bx[t][6] = v1.z; bx[t][7] = v1.w;
+          }
+          #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t a01, a23, b01, b23;
+            dec_w8(wA[j], a01, a23);
+            dec_w8(wB[j], b01, b23);
+            #pragma unroll
+            for (int t = 0; t < MT; ++t) mma_16816(acc[t], a01, b01, a23, b23, bx[t][2 * j], bx[t][2 * j + 1]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+  }
+
+  // ---------------------------------------------- intra-CTA reduction
+  named_bar_sync(1, nct);          // every consumer is done reading the ring
+  float* red = reinterpret_cast<float*>(ring);     // [tpc][wpt][MC][16]
+  {
+    float* mine = red + (size_t)(tt * wpt + w) * MC * kTileRows;
+    #pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int mm = t * 8 + 2 * c;
+      mine[(mm + 0) * kTileRows + prow] = acc[t][0];
+      mine[(mm + 1) * kTileRows + prow] = acc[t][1];
+      mine[(mm + 0) * kTileRows + prow + 8] = acc[t][2];
+      mine[(mm + 1) * kTileRows + prow + 8] = acc[t][3];
+    }
+  }
+  named_bar_sync(1, nct);
+
+  const int nout = MC * rows_cta;   // (m, r) pairs of this CTA, r fastest
+  if (p.ks == 1) {
+    for (int idx = ctid; idx < nout; idx += nct) {
+      const int m = idx / rows_cta, r = idx - m * rows_cta;
+      const int t = r >> 4, rr = r & 15;
+      float v = 0.f;
+      for (int w2 = 0; w2 < wpt; ++w2) v += red[((size_t)(t * wpt + w2) * MC + m) * kTileRows + rr];
+      const int n = row0 + r, mm = m0 + m;
+      if (n < p.N && mm < p.M) p.out[(long long)mm * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+    }
+    return;
+  }
+
+  // ----------------------------------------- cross-CTA split-K reduction
+  const size_t slot_elems = (size_t)MC * rows_cta;
+  const size_t tile_id = (size_t)mchunk * gridDim.x + blk;
+  float* slots = p.partials + tile_id * p.ks * slot_elems;
+  {
+    float* mine = slots + (size_t)split * slot_elems;
+    for (int idx = ctid; idx < nout; idx += nct) {
+      const int m = idx / rows_cta, r = idx - m * rows_cta;
+      const int t = r >> 4, rr = r & 15;
+      float v = 0.f;
+      for (int w2 = 0; w2 < wpt; ++w2) v += red[((size_t)(t * wpt + w2) * MC + m) * kTileRows + rr];
+      mine[idx] = v;
+    }
+  }
+  __threadfence();
+  named_bar_sync(1, nct);
+  if (ctid == 0) {
+    const unsigned old = atomicAdd(p.counters + tile_id, 1u);
+    *last_flag = (old == (unsigned)(p.ks - 1));
+  }
+  named_bar_sync(1, nct);
+  if (*last_flag) {
+    __threadfence();
+    for (int idx = ctid; idx < nout; idx += nct) {
+      float v = 0.f;
+      for (int s2 = 0; s2 < p.ks; ++s2) v += __ldcg(slots + (size_t)s2 * slot_elems + idx);
+      const int m = idx / rows_cta, r = idx - m * rows_cta;
+      const int n = row0 + r, mm = m0 + m;
+      if (n < p.N && mm < p.M) p.out[(long long)mm * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+    }
+    if (ctid == 0) p.counters[tile_id] = 0u;     // leave the workspace zeroed
+  }
+}
+
+}  // namespace gemv
+}  // namespace ql

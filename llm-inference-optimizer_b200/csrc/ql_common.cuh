@@ -1,0 +1,210 @@
+// ql_common.cuh — device helpers shared by the qlinear kernels (sm_100a).
+//
+// Inline-PTX wrappers for mbarriers, TMA bulk-tensor loads, programmatic
+// dependent launch, named barriers and mma.sync, plus the register-level
+// decoders that turn packed int4 / int8 weights into exact fp16 pairs.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace ql {
+
+// ------------------------------------------------------------------ errors
+// Device-global error word.  A kernel whose bounded wait runs out stores a
+// code here (first writer wins) and carries on without trapping.
+enum DeviceError : unsigned {
+  kDevErrNone = 0,
+  kDevErrFullWait = 1,      // consumer waited too long for a TMA stage
+  kDevErrEmptyWait = 2,     // producer waited too long for a free stage
+  kDevErrMmaWait = 3,       // tensor-core completion wait ran out
+  kDevErrTmem = 4,          // TMEM allocation failed
+};
+
+// Wall-clock budget of any single bounded wait (nanoseconds, %globaltimer).
+constexpr unsigned long long kWaitBudgetNs = 2000000000ull;   // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------------------ addressing
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// --------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  // make the initialised barriers visible to the async (TMA) proxy
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on the phase with the given parity.  Returns false (and
+// records `code` in the device error word) when the budget runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word,
+                                          unsigned code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    #pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+      atomicCAS(err_word, 0u, code);
+      return false;
+    }
+  }
+}
+
+// -------------------------------------------------------------------- TMA
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// 2-D tiled bulk-tensor load global -> shared, completion on an mbarrier.
+// No cluster multicast anywhere in this library.
+__device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap* tm, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------- programmatic dependent launch
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------- named barriers
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------ memory ops
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ------------------------------------------------------------- tensor ops
+// D(16x8,f32) += A(16x16,f16,row) * B(16x8,f16,col)
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------- weight decoders
+// All decoders build fp16 values with the exponent of 1024 ("magic number"
+// construction: 0x6400 | v is the half 1024 + v for 0 <= v < 1024) and
+// subtract the offset in half precision.  Every intermediate is an integer
+// below 2048, so each result is the exact small integer.
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t bits) {
+  uint32_t r;
+  // r = (a & mask) | bits   (truth table 0xEA)
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bits));
+  return r;
+}
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b),
+                      *reinterpret_cast<__half2*>(&c));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+constexpr uint32_t kH2Magic = 0x64006400u;     // (1024, 1024)
+constexpr uint32_t kH2_1032 = 0x64086408u;     // (1032, 1032): 1024 + 8
+constexpr uint32_t kH2_1152 = 0x64806480u;     // (1152, 1152): 1024 + 128
+constexpr uint32_t kH2_1_16 = 0x2C002C00u;     // (1/16, 1/16)
+constexpr uint32_t kH2_m72 = 0xD480D480u;      // (-72, -72): 64 + 8
+
+// Split-half int4 (the reference's layout).  u holds 4 consecutive packed
+// bytes b0..b3 of one group; their low nibbles are k = j..j+3 and their high
+// nibbles k = j+64..j+67.  Outputs are (q-8) as half2 pairs:
+//   lo01 = (k j,   k j+1)     lo23 = (k j+2,  k j+3)
+//   hi01 = (k j+64, k j+65)   hi23 = (k j+66, k j+67)
+__device__ __forceinline__ void dec_w4_split(uint32_t u, uint32_t& lo01, uint32_t& lo23,
+                                             uint32_t& hi01, uint32_t& hi23) {
+  const uint32_t t0 = __byte_perm(u, 0u, 0x1100);   // byte0 = b0, byte2 = b1
+  const uint32_t t1 = __byte_perm(u, 0u, 0x3322);   // byte0 = b2, byte2 = b3
+  lo01 = h2_sub(lop3_and_or(t0, 0x000F000Fu, kH2Magic), kH2_1032);
+  lo23 = h2_sub(lop3_and_or(t1, 0x000F000Fu, kH2Magic), kH2_1032);
+  // (1024 + 16 h) / 16 - 72 = h - 8
+  hi01 = h2_fma(lop3_and_or(t0, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+  hi23 = h2_fma(lop3_and_or(t1, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+}
+
+// Adjacent-pair int4: byte i holds k = 2i (low nibble) and 2i+1 (high).
+// u = bytes b0..b3 -> k 0..7; outputs p01 = (k0,k1), p23, p45, p67.
+__device__ __forceinline__ void dec_w4_adjacent(uint32_t u, uint32_t& p01, uint32_t& p23,
+                                                uint32_t& p45, uint32_t& p67) {
+  const uint32_t v = u >> 4;
+  p01 = h2_sub(lop3_and_or(__byte_perm(u, v, 0x4400), 0x000F000Fu, kH2Magic), kH2_1032);
+  p23 = h2_sub(lop3_and_or(__byte_perm(u, v, 0x5511), 0x000F000Fu, kH2Magic), kH2_1032);
+  p45 = h2_sub(lop3_and_or(__byte_perm(u, v, 0x6622), 0x000F000Fu, kH2Magic), kH2_1032);
+  p67 = h2_sub(lop3_and_or(__byte_perm(u, v, 0x7733), 0x000F000Fu, kH2Magic), kH2_1032);
+}
+
+// int8: u = 4 signed bytes (k 0..3) -> p01 = (k0,k1), p23 = (k2,k3), exact.
+__device__ __forceinline__ void dec_w8(uint32_t u, uint32_t& p01, uint32_t& p23) {
+  const uint32_t v = u ^ 0x80808080u;                      // b + 128 in 0..255
+  p01 = h2_sub(__byte_perm(v, 0x64646464u, 0x4140), kH2_1152);
+  p23 = h2_sub(__byte_perm(v, 0x64646464u, 0x4342), kH2_1152);
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t h) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+}  // namespace ql

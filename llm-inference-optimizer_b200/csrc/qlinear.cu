@@ -1,0 +1,535 @@
+// qlinear.cu — C ABI of libqlinear.so (declared in include/qlinear.h).
+//
+// Host side of the B200 weight-only quantized linear layer: argument
+// checks, the shape-based kernel plan (fixed heuristic, no autotuning, so a
+// first call can be recorded into a CUDA graph), TMA descriptor encoding and
+// the launches.  Every entry point returns a status and allocates nothing.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/qlinear.h"
+#include "ql_common.cuh"
+#include "qformat.cuh"
+#include "qgemv.cuh"
+
+#define QL_VERSION_MAJOR 0
+#define QL_VERSION_MINOR 1
+#define QL_VERSION_PATCH 0
+
+// Device-global error word written by bounded waits that run out.
+__device__ unsigned g_ql_device_error;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr size_t kSmemOptin = 232448;   // 227 KB dynamic shared memory per block on sm_100
+
+struct DeviceInfo {
+  std::once_flag once;
+  int status = QL_OK;
+  int sms = 0;
+  unsigned* err_word = nullptr;
+};
+DeviceInfo g_dev[kMaxDevices];
+
+int init_device(int dev) {
+  int major = 0, minor = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  if (major != 10) return QL_ERR_DEVICE;   // built for sm_100a only
+  g_dev[dev].sms = sms;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_ql_device_error) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  g_dev[dev].err_word = static_cast<unsigned*>(p);
+  return QL_OK;
+}
+
+// Returns the current device's info, or nullptr with *status set.
+DeviceInfo* current_device(int* status) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    *status = QL_ERR_DEVICE;
+    return nullptr;
+  }
+  DeviceInfo& d = g_dev[dev];
+  std::call_once(d.once, [&] { d.status = init_device(dev); });
+  *status = d.status;
+  return d.status == QL_OK ? &d : nullptr;
+}
+
+// ------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2-D uint8 map over rows of `inner_bytes` valid bytes, 128-byte swizzle.
+int make_weight_map(CUtensorMap* tm, const void* base, uint64_t inner_bytes, uint64_t rows,
+                    uint64_t row_stride, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return QL_ERR_DEVICE;
+  cuuint64_t dims[2] = {inner_bytes, rows};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
+}
+
+// ------------------------------------------------------------- launch
+template <typename Kern, typename... Args>
+int launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  return QL_OK;
+}
+
+// Raise the dynamic shared-memory limit of a kernel once per device.
+template <typename Kern>
+int allow_smem(Kern kernel, int slot) {
+  static std::atomic<unsigned char> done[kMaxDevices][16];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (done[dev][slot].load(std::memory_order_acquire)) return QL_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  done[dev][slot].store(1, std::memory_order_release);
+  return QL_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ------------------------------------------------------------- GEMV plan
+struct GemvPlan {
+  int tpc = 0, wpt = 0, ks = 0, kbps = 0, stages = 0, mt = 0, mchunks = 0;
+  int x_stride = 0, x_rows = 0, nblk = 0, nkb = 0;
+  size_t smem = 0, ws_bytes = 0, ws_counters = 0;
+  double cost = 0;
+};
+
+size_t gemv_ws_bytes(const GemvPlan& p) {
+  if (p.ks <= 1) return 0;
+  const size_t counters = ((size_t)p.nblk * p.mchunks * 4 + 255) / 256 * 256;
+  const size_t partials = (size_t)p.nblk * p.mchunks * p.ks * (8 * p.mt) * (p.tpc * 16) * 4;
+  return counters + partials;
+}
+
+// Optional override for tuning sweeps: QLINEAR_GEMV_PLAN="tpc,ks" (ks = 0
+// lets the planner choose).  Read once.
+void plan_override(int* tpc, int* ks) {
+  static int o_tpc = -1, o_ks = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = std::getenv("QLINEAR_GEMV_PLAN");
+    if (e && std::sscanf(e, "%d,%d", &o_tpc, &o_ks) != 2) o_tpc = o_ks = -1;
+  });
+  *tpc = o_tpc;
+  *ks = o_ks;
+}
+
+// Fixed, shape-based plan (no autotuning).  Cost model: one CTA per SM at a
+// time; an SM streams its CTAs' weight slices at the per-SM share of HBM
+// bandwidth (capped); each wave pays a fixed latency; split-K pays a
+// reduction.  Returns false if no plan fits.
+bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, GemvPlan* out) {
+  const int mt = M <= 8 ? 1 : 2;
+  const int mc = 8 * mt;
+  const int64_t kbytes = wbits == 4 ? K / 2 : K;
+  const int nkb = (int)cdiv(kbytes, 128);
+  const int epk = wbits == 4 ? 256 : 128;
+  const int64_t NT = cdiv(N, 16);
+  const int x_rows = (int)std::min<int64_t>(mc, M);
+  const int mchunks = (int)cdiv(M, mc);
+  const double bw_total = 6.5e12, bw_sm_max = 120e9, t_wave = 1.5e-6, t_red = 0.8e-6;
+  int o_tpc, o_ks;
+  plan_override(&o_tpc, &o_ks);
+
+  GemvPlan best;
+  best.cost = 1e30;
+  bool found = false;
+  for (int tpc : {1, 2, 4, 8}) {
+    if (o_tpc > 0 && tpc != o_tpc) continue;
+    if (tpc > 1 && (int64_t)(tpc / 2) * 16 >= N) continue;
+    const int64_t nblk = cdiv(NT, tpc);
+    int last_kbps = -1;
+    for (int ks = 1; ks <= nkb; ++ks) {
+      const int kbps = (int)cdiv(nkb, ks);
+      if (kbps == last_kbps) continue;
+      last_kbps = kbps;
+      const int ks_eff = (int)cdiv(nkb, kbps);
+      if (o_ks > 0 && ks_eff != o_ks) continue;
+      GemvPlan p;
+      p.tpc = tpc;
+      p.ks = ks_eff;
+      p.kbps = kbps;
+      p.mt = mt;
+      p.mchunks = mchunks;
+      p.nblk = (int)nblk;
+      p.nkb = nkb;
+      p.x_stride = kbps * epk + 8;
+      p.x_rows = x_rows;
+      p.wpt = std::min(kbps, ql::gemv::kMaxConsumerWarps / tpc);
+      if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
+      p.ws_bytes = gemv_ws_bytes(p);
+      if (p.ws_bytes > ws_avail) continue;
+      if (nblk * ks_eff * mchunks > INT_MAX / 2) continue;
+      // ring depth: as many stages as fit, up to the whole slice
+      const size_t box = (size_t)tpc * 16 * 128;
+      const ql::gemv::Smem base = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, p.x_stride, kbps);
+      const size_t fixed = base.total - base.region0 + 2 * 8 * 32;
+      const int fit = (int)std::min<size_t>(32, (kSmemOptin - fixed) / box);
+      p.stages = std::min(kbps, fit);
+      if (p.stages < std::min(kbps, 2)) continue;
+      p.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, p.stages, p.x_stride, kbps).total;
+      if (p.smem > kSmemOptin) continue;
+      const double ctas = (double)nblk * ks_eff * mchunks;
+      const double waves = std::ceil(ctas / sms);
+      const double active = std::min<double>(ctas, sms);
+      const double cta_bytes = (double)tpc * 16 * kbps * 128;
+      const double bw_sm = std::min(bw_total / active, bw_sm_max);
+      p.cost = waves * (cta_bytes / bw_sm + t_wave) + (ks_eff > 1 ? t_red : 0.0);
+      if (p.cost < best.cost * 0.999) {
+        best = p;
+        found = true;
+      }
+    }
+  }
+  if (found) *out = best;
+  return found;
+}
+
+template <int WBITS, int LAYOUT, int MT>
+int launch_gemv_t(const GemvPlan& pl, const CUtensorMap& tm, const ql::gemv::Params& prm, cudaStream_t s,
+                  bool pdl) {
+  auto kern = ql::gemv::qgemv_kernel<WBITS, LAYOUT, MT>;
+  const int slot = (WBITS == 4 ? 0 : 8) + LAYOUT * 4 + MT;
+  int st = allow_smem(kern, slot);
+  if (st != QL_OK) return st;
+  dim3 grid(pl.nblk, pl.ks, pl.mchunks);
+  dim3 block((pl.tpc * pl.wpt + 1) * 32);
+  return launch(kern, grid, block, pl.smem, s, pdl, tm, prm);
+}
+
+struct LinearArgs {
+  int wbits;
+  const void* x;
+  const void* w;
+  int layout;
+  const void* scale;
+  int scale_dtype;
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int64_t M, N, K, ldx, ldw, lds, ldo;
+  void* ws;
+  size_t ws_bytes;
+  unsigned flags;
+  cudaStream_t stream;
+};
+
+int run_generic(const LinearArgs& a) {
+  ql::fmt::GenericParams p;
+  p.x = static_cast<const __half*>(a.x);
+  p.w = a.w;
+  p.scale = a.scale;
+  p.bias = a.bias;
+  p.out = static_cast<__half*>(a.out);
+  p.ldx = a.ldx;
+  p.ldw = a.ldw;
+  p.lds = a.lds;
+  p.ldo = a.ldo;
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
+  p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  p.layout = a.layout;
+  dim3 grid((unsigned)cdiv(a.N, 8), (unsigned)cdiv(a.M, 8));
+  if (grid.y > 65535) return QL_ERR_BAD_SHAPE;
+  if (a.wbits == 8) return launch(ql::fmt::qlinear_generic_kernel<8>, grid, dim3(256), 0, a.stream, false, p);
+  return launch(ql::fmt::qlinear_generic_kernel<4>, grid, dim3(256), 0, a.stream, false, p);
+}
+
+int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
+  GemvPlan pl;
+  const size_t avail = a.ws ? a.ws_bytes : 0;
+  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return QL_ERR_UNSUPPORTED;
+  CUtensorMap tm;
+  const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
+  int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, (uint32_t)(pl.tpc * 16));
+  if (st != QL_OK) return st;
+  ql::gemv::Params p;
+  p.x = static_cast<const __half*>(a.x);
+  p.scale = a.scale;
+  p.bias = a.bias;
+  p.out = static_cast<__half*>(a.out);
+  p.ldx = a.ldx;
+  p.lds = a.lds;
+  p.ldo = a.ldo;
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.kbytes = (int)kbytes;
+  p.nkb = pl.nkb;
+  p.kb_per_split = pl.kbps;
+  p.ks = pl.ks;
+  p.tpc = pl.tpc;
+  p.wpt = pl.wpt;
+  p.stages = pl.stages;
+  p.x_stride = pl.x_stride;
+  p.x_rows = pl.x_rows;
+  p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
+  p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
+  p.early_weights = pdl ? 1 : 0;
+  p.err = dev->err_word;
+  if (pl.ks > 1) {
+    const size_t counters = ((size_t)pl.nblk * pl.mchunks * 4 + 255) / 256 * 256;
+    p.counters = static_cast<uint32_t*>(a.ws);
+    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + counters);
+  } else {
+    p.counters = nullptr;
+    p.partials = nullptr;
+  }
+  if (a.wbits == 8) {
+    return pl.mt == 1 ? launch_gemv_t<8, 0, 1>(pl, tm, p, a.stream, pdl)
+                      : launch_gemv_t<8, 0, 2>(pl, tm, p, a.stream, pdl);
+  }
+  if (a.layout == QL_W4_LAYOUT_SPLIT_HALF)
+    return pl.mt == 1 ? launch_gemv_t<4, 0, 1>(pl, tm, p, a.stream, pdl)
+                      : launch_gemv_t<4, 0, 2>(pl, tm, p, a.stream, pdl);
+  return pl.mt == 1 ? launch_gemv_t<4, 1, 1>(pl, tm, p, a.stream, pdl)
+                    : launch_gemv_t<4, 1, 2>(pl, tm, p, a.stream, pdl);
+}
+
+int run_linear(const LinearArgs& a) {
+  if (!a.x || !a.w || !a.scale || !a.out) {
+    if (a.M == 0 || a.N == 0) return QL_OK;
+    return QL_ERR_NULL_POINTER;
+  }
+  if (a.M < 0 || a.N < 0 || a.K < 0) return QL_ERR_BAD_SHAPE;
+  if (a.M > INT_MAX || a.N > INT_MAX || a.K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (a.wbits == 4 && a.K % 128 != 0) return QL_ERR_BAD_SHAPE;
+  if (a.M == 0 || a.N == 0) return QL_OK;
+  const int64_t wrow = a.wbits == 4 ? a.K / 2 : a.K;
+  if (a.ldx < a.K || a.ldw < wrow || a.ldo < a.N) return QL_ERR_BAD_STRIDE;
+  if (a.wbits == 4 && a.lds < a.N) return QL_ERR_BAD_STRIDE;
+  if (a.scale_dtype != QL_DTYPE_F32 && a.scale_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (a.wbits == 4 && a.scale_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (a.bias && a.bias_dtype != QL_DTYPE_F16 && a.bias_dtype != QL_DTYPE_F32) return QL_ERR_UNSUPPORTED;
+  if (a.wbits == 4 && a.layout != QL_W4_LAYOUT_SPLIT_HALF && a.layout != QL_W4_LAYOUT_ADJACENT)
+    return QL_ERR_UNSUPPORTED;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  if (a.flags & QL_FLAG_FORCE_GEMM) return QL_ERR_UNSUPPORTED;
+  const bool fast_ok = a.K > 0 && aligned16(a.x) && a.ldx % 8 == 0 && a.K % 8 == 0 && aligned16(a.w) &&
+                       a.ldw % 16 == 0 && wrow % 16 == 0;
+  if ((a.flags & QL_FLAG_FORCE_GENERIC) || !fast_ok) return run_generic(a);
+  return run_gemv(a, dev);
+}
+
+}  // namespace
+
+// ======================================================================
+extern "C" {
+
+int ql_w8a16_linear(const void* x, int x_dtype, const void* w_q, const void* scale, int scale_dtype,
+                    const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                    int64_t ldw, int64_t ldo, void* workspace, size_t workspace_bytes, unsigned flags,
+                    void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  LinearArgs a{8, x, w_q, 0, scale, scale_dtype, bias, bias_dtype, out, M, N, K, ldx, ldw, 0, ldo,
+               workspace, workspace_bytes, flags, static_cast<cudaStream_t>(stream)};
+  return run_linear(a);
+}
+
+int ql_w4a16_linear(const void* x, int x_dtype, const void* w_packed, int layout, const void* scales,
+                    const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                    int64_t ldw, int64_t lds, int64_t ldo, void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, out, M, N, K, ldx, ldw, lds,
+               ldo, workspace, workspace_bytes, flags, static_cast<cudaStream_t>(stream)};
+  return run_linear(a);
+}
+
+static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || (wbits == 4 && K % 128 != 0)) return 0;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return 0;
+  GemvPlan pl;
+  if (!plan_gemv(wbits, M, N, K, dev->sms, SIZE_MAX, &pl)) return 0;
+  return pl.ws_bytes;
+}
+
+size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(8, M, N, K); }
+size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }
+
+int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype, float* out, int64_t N, int64_t K,
+                        int64_t ldw, void* stream) {
+  if (N == 0 || K == 0) return QL_OK;
+  if (!w_q || !scale || !out) return QL_ERR_NULL_POINTER;
+  if (N < 0 || K < 0 || N > INT_MAX || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (ldw < K) return QL_ERR_BAD_STRIDE;
+  if (scale_dtype != QL_DTYPE_F32 && scale_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  int st;
+  if (!current_device(&st)) return st;
+  const int vec_ok = (reinterpret_cast<uintptr_t>(w_q) % 4 == 0) && ldw % 4 == 0;
+  const long long total = N * ((K + 3) / 4);
+  const unsigned blocks = (unsigned)cdiv(total, 256);
+  return launch(ql::fmt::dequant_int8_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                false, static_cast<const int8_t*>(w_q), scale, (int)(scale_dtype == QL_DTYPE_F32), out, (int)N,
+                (int)K, (long long)ldw, vec_ok);
+}
+
+int ql_w4a16_dequantize(const void* w_packed, int layout, const void* scales, float* out, int64_t N, int64_t K,
+                        int64_t ldw, int64_t lds, void* stream) {
+  if (N == 0 || K == 0) return QL_OK;
+  if (!w_packed || !scales || !out) return QL_ERR_NULL_POINTER;
+  if (N < 0 || K < 0 || K % 128 != 0 || N > INT_MAX || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (ldw < K / 2 || lds < N) return QL_ERR_BAD_STRIDE;
+  if (layout != QL_W4_LAYOUT_SPLIT_HALF && layout != QL_W4_LAYOUT_ADJACENT) return QL_ERR_UNSUPPORTED;
+  int st;
+  if (!current_device(&st)) return st;
+  const int vec_ok = (reinterpret_cast<uintptr_t>(w_packed) % 4 == 0) && ldw % 4 == 0;
+  const long long total = N * (K / 8);
+  const unsigned blocks = (unsigned)cdiv(total, 256);
+  return launch(ql::fmt::dequant_int4_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                false, static_cast<const uint8_t*>(w_packed), layout, static_cast<const __half*>(scales), out,
+                (int)N, (int)K, (long long)ldw, (long long)lds, vec_ok);
+}
+
+int ql_w4a16_unpack(const void* w_packed, int layout, uint8_t* out, int64_t N, int64_t K, int64_t ldw,
+                    void* stream) {
+  if (N == 0 || K == 0) return QL_OK;
+  if (!w_packed || !out) return QL_ERR_NULL_POINTER;
+  if (N < 0 || K < 0 || K % 2 != 0 || N > INT_MAX || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (layout == QL_W4_LAYOUT_SPLIT_HALF && K % 128 != 0) return QL_ERR_BAD_SHAPE;
+  if (ldw < K / 2) return QL_ERR_BAD_STRIDE;
+  if (layout != QL_W4_LAYOUT_SPLIT_HALF && layout != QL_W4_LAYOUT_ADJACENT) return QL_ERR_UNSUPPORTED;
+  int st;
+  if (!current_device(&st)) return st;
+  const long long total = N * K;
+  return launch(ql::fmt::unpack_int4_kernel, dim3((unsigned)cdiv(total, 256)), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), false, static_cast<const uint8_t*>(w_packed), layout, out,
+                (int)N, (int)K, (long long)ldw);
+}
+
+int ql_w8a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int8_t* w_q, float* scale,
+                      void* stream) {
+  if (N == 0) return QL_OK;
+  if (!w || !w_q || !scale) return QL_ERR_NULL_POINTER;
+  if (N < 0 || K < 0 || N > INT_MAX || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (ldw < K) return QL_ERR_BAD_STRIDE;
+  int st;
+  if (!current_device(&st)) return st;
+  return launch(ql::fmt::quantize_int8_kernel, dim3((unsigned)N), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), false, static_cast<const __half*>(w), (long long)ldw, (int)K,
+                w_q, scale);
+}
+
+int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int qmin, int layout, uint8_t* w_packed,
+                      void* scales, void* stream) {
+  if (N == 0 || K == 0) return QL_OK;
+  if (!w || !w_packed || !scales) return QL_ERR_NULL_POINTER;
+  if (N < 0 || K < 0 || K % 128 != 0 || N > 65535 || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (ldw < K) return QL_ERR_BAD_STRIDE;
+  if (qmin < -8 || qmin > 0) return QL_ERR_UNSUPPORTED;
+  if (layout != QL_W4_LAYOUT_SPLIT_HALF && layout != QL_W4_LAYOUT_ADJACENT) return QL_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(w_packed) % 4 != 0) return QL_ERR_UNSUPPORTED;
+  int st;
+  if (!current_device(&st)) return st;
+  const int G = (int)(K / 128);
+  return launch(ql::fmt::quantize_int4_kernel, dim3((unsigned)cdiv(G, 4), (unsigned)N), dim3(128), 0,
+                static_cast<cudaStream_t>(stream), false, static_cast<const __half*>(w), (long long)ldw, (int)K,
+                qmin, layout, w_packed, static_cast<__half*>(scales), (int)N);
+}
+
+const char* ql_strerror(int status) {
+  switch (status) {
+    case QL_OK: return "ok";
+    case QL_ERR_NULL_POINTER: return "qlinear: a required pointer is NULL";
+    case QL_ERR_BAD_SHAPE: return "qlinear: unsupported or invalid shape";
+    case QL_ERR_BAD_STRIDE: return "qlinear: leading dimension smaller than the row length";
+    case QL_ERR_UNSUPPORTED: return "qlinear: dtype, layout, flag or alignment not supported by this build";
+    case QL_ERR_WORKSPACE: return "qlinear: workspace too small";
+    case QL_ERR_CUDA: return "qlinear: CUDA runtime call failed";
+    case QL_ERR_DEVICE: return "qlinear: no usable sm_100 device (this library is built for B200 / sm_100a)";
+    case QL_ERR_DEVICE_TIMEOUT: return "qlinear: a kernel gave up a bounded wait";
+    default: return "qlinear: unknown status";
+  }
+}
+
+int ql_version(void) { return (QL_VERSION_MAJOR << 16) | (QL_VERSION_MINOR << 8) | QL_VERSION_PATCH; }
+
+int ql_device_error(int* code_out) {
+  if (!code_out) return QL_ERR_NULL_POINTER;
+  int st;
+  if (!current_device(&st)) return st;
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_ql_device_error, sizeof(v)) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  *code_out = (int)v;
+  return QL_OK;
+}
+
+int ql_clear_device_error(void) {
+  int st;
+  if (!current_device(&st)) return st;
+  const unsigned zero = 0;
+  if (cudaMemcpyToSymbol(g_ql_device_error, &zero, sizeof(zero)) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  return QL_OK;
+}
+
+}  // extern "C"
