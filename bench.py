@@ -412,6 +412,35 @@ def run_ours(args):
     return 0
 
 
+def run_profile_one(args):
+    """A handful of eager launches of one (wbits, M, K, N) layer with its
+    weights cycled over enough copies to exceed L2: the small case that the
+    ncu captures in profiles/ are taken on."""
+    import torch
+
+    from qlinear.kernels.w4a16_matmul import w4a16_linear, w4a16_quantize_cuda
+    from qlinear.kernels.w8a16_matmul import w8a16_linear, w8a16_quantize_cuda
+    parts = [int(v) for v in args.profile_one.split(",")]
+    wbits, M, K, N = parts
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    per = N * K // (2 if wbits == 4 else 1)
+    copies = max(2, int(300e6 // max(per, 1)) + 1)
+    layers = []
+    for _ in range(copies):
+        w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+        layers.append(w4a16_quantize_cuda(w) if wbits == 4 else w8a16_quantize_cuda(w))
+        del w
+    x = torch.randn(M, K, generator=gen, device=dev).half()
+    for i in range(args.steps):
+        a, b = layers[i % copies]
+        (w4a16_linear if wbits == 4 else w8a16_linear)(x, a, b)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_one": args.profile_one, "launches": args.steps, "copies": copies}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,7 +449,11 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
+                    help="a few eager launches of one layer shape (small case for ncu)")
     args = ap.parse_args()
+    if args.profile_one:
+        return run_profile_one(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

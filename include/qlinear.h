@@ -127,6 +127,16 @@ int ql_w4a16_linear(const void* x, int x_dtype,
 size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
 
+/* The decode-kernel plan the library would use for (wbits, M, N, K) with a
+ * workspace of `workspace_bytes` (SIZE_MAX = unlimited), for tuning and
+ * tests.  fields[0..9] = tiles of 16 rows per CTA, consumer warps per tile,
+ * K-splits, 128-byte k-blocks per split, ring stages, batch tiles of 8 per
+ * CTA, batch chunks, CTAs, dynamic shared bytes, workspace bytes.  Has no
+ * counterpart in the reference (its Triton configs are fixed in
+ * _pick_config, w8a16_matmul_triton.py:89-99). */
+int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes,
+                 int64_t* fields, int nfields);
+
 /* -------------------------------------------------------- format helpers */
 /* out_f32[N, K] = w_q * scale (fp32), bit-exact with the reference. */
 int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype,

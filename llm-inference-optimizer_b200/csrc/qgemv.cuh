@@ -35,7 +35,10 @@ namespace gemv {
 
 constexpr int kTileRows = 16;
 constexpr int kBlockBytes = 128;    // k-block width = TMA box inner extent (SW128)
-constexpr int kMaxConsumerWarps = 16;
+// At most 8 consumer warps + 1 producer warp, so that two CTAs fit on an SM
+// by registers: the next kernel's CTAs can then start streaming their
+// weights (programmatic dependent launch) while this kernel finishes.
+constexpr int kMaxConsumerWarps = 8;
 constexpr int kMaxThreads = (kMaxConsumerWarps + 1) * 32;
 
 struct Params {
@@ -96,7 +99,7 @@ __device__ __forceinline__ float finish_value(const Params& p, float v, int n) {
 
 // MT = number of n8 batch tiles per CTA (mc = 8*MT batch rows per grid.z slice).
 template <int WBITS, int LAYOUT, int MT>
-__global__ void __launch_bounds__(kMaxThreads, 1)
+__global__ void __launch_bounds__(kMaxThreads, 2)
     qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const Params p) {
   constexpr int MC = 8 * MT;
   constexpr int EPK = WBITS == 4 ? 256 : 128;      // k elements per k-block
@@ -370,7 +373,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     __threadfence();
     for (int idx = ctid; idx < nout; idx += nct) {
       float v = 0.f;
-      for (int s2 = 0; s2 < p.ks; ++s2) v += __ldcg(slots + (size_t)s2 * slot_elems + idx);
+      for (int s2 = 0; s2 < p.ks; ++s2) {
+        float* slot = slots + (size_t)s2 * slot_elems + idx;
+        v += __ldcg(slot);
+        __stcg(slot, 0.f);                       // leave the workspace zeroed
+      }
       const int m = idx / rows_cta, r = idx - m * rows_cta;
       const int n = row0 + r, mm = m0 + m;
       if (n < p.N && mm < p.M) p.out[(long long)mm * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));

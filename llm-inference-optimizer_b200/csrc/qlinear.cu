@@ -171,10 +171,13 @@ void plan_override(int* tpc, int* ks) {
   *ks = o_ks;
 }
 
-// Fixed, shape-based plan (no autotuning).  Cost model: one CTA per SM at a
-// time; an SM streams its CTAs' weight slices at the per-SM share of HBM
-// bandwidth (capped); each wave pays a fixed latency; split-K pays a
-// reduction.  Returns false if no plan fits.
+// Fixed, shape-based plan (no autotuning).  Cost model: CTAs are spread over
+// the SMs; an SM streams its CTAs' weight slices at its share of HBM
+// bandwidth (capped per SM); each wave pays a fixed latency; split-K pays a
+// reduction; a CTA too big to share its SM with the next kernel's CTA (no
+// overlap under programmatic dependent launch) pays a penalty.
+constexpr size_t kSmemShared = 110 * 1024;   // two CTAs per SM fit under this
+
 bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, GemvPlan* out) {
   const int mt = M <= 8 ? 1 : 2;
   const int mc = 8 * mt;
@@ -184,7 +187,8 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   const int64_t NT = cdiv(N, 16);
   const int x_rows = (int)std::min<int64_t>(mc, M);
   const int mchunks = (int)cdiv(M, mc);
-  const double bw_total = 6.5e12, bw_sm_max = 120e9, t_wave = 1.5e-6, t_red = 0.8e-6;
+  if (mchunks > 65535) return false;
+  const double bw_total = 6.5e12, bw_sm_max = 120e9, t_wave = 1.5e-6, t_red = 0.8e-6, t_big = 0.8e-6;
   int o_tpc, o_ks;
   plan_override(&o_tpc, &o_ks);
 
@@ -193,8 +197,9 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   bool found = false;
   for (int tpc : {1, 2, 4, 8}) {
     if (o_tpc > 0 && tpc != o_tpc) continue;
-    if (tpc > 1 && (int64_t)(tpc / 2) * 16 >= N) continue;
+    if (o_tpc <= 0 && tpc > 1 && (int64_t)(tpc / 2) * 16 >= N) continue;
     const int64_t nblk = cdiv(NT, tpc);
+    if (nblk > INT_MAX / 2) continue;
     int last_kbps = -1;
     for (int ks = 1; ks <= nkb; ++ks) {
       const int kbps = (int)cdiv(nkb, ks);
@@ -202,6 +207,7 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       last_kbps = kbps;
       const int ks_eff = (int)cdiv(nkb, kbps);
       if (o_ks > 0 && ks_eff != o_ks) continue;
+      if (ks_eff > 65535) continue;
       GemvPlan p;
       p.tpc = tpc;
       p.ks = ks_eff;
@@ -216,12 +222,13 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
       p.ws_bytes = gemv_ws_bytes(p);
       if (p.ws_bytes > ws_avail) continue;
-      if (nblk * ks_eff * mchunks > INT_MAX / 2) continue;
-      // ring depth: as many stages as fit, up to the whole slice
+      // ring depth: the whole slice if it fits next to a second CTA, else
+      // as many stages as fit at all
       const size_t box = (size_t)tpc * 16 * 128;
       const ql::gemv::Smem base = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, p.x_stride, kbps);
       const size_t fixed = base.total - base.region0 + 2 * 8 * 32;
-      const int fit = (int)std::min<size_t>(32, (kSmemOptin - fixed) / box);
+      int fit = kSmemShared > fixed ? (int)std::min<size_t>(32, (kSmemShared - fixed) / box) : 0;
+      if (fit < std::min(kbps, 2)) fit = (int)std::min<size_t>(32, (kSmemOptin - fixed) / box);
       p.stages = std::min(kbps, fit);
       if (p.stages < std::min(kbps, 2)) continue;
       p.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, p.stages, p.x_stride, kbps).total;
@@ -231,7 +238,8 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       const double active = std::min<double>(ctas, sms);
       const double cta_bytes = (double)tpc * 16 * kbps * 128;
       const double bw_sm = std::min(bw_total / active, bw_sm_max);
-      p.cost = waves * (cta_bytes / bw_sm + t_wave) + (ks_eff > 1 ? t_red : 0.0);
+      p.cost = waves * (cta_bytes / bw_sm + t_wave) + (ks_eff > 1 ? t_red : 0.0) +
+               (p.smem > kSmemShared ? t_big : 0.0);
       if (p.cost < best.cost * 0.999) {
         best = p;
         found = true;
@@ -294,10 +302,14 @@ int run_generic(const LinearArgs& a) {
   return launch(ql::fmt::qlinear_generic_kernel<4>, grid, dim3(256), 0, a.stream, false, p);
 }
 
+int run_generic(const LinearArgs& a);
+
 int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   GemvPlan pl;
   const size_t avail = a.ws ? a.ws_bytes : 0;
-  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return QL_ERR_UNSUPPORTED;
+  // no decode plan fits (e.g. a tall K with many batch rows and no
+  // workspace for split-K): the portable kernel takes it
+  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return run_generic(a);
   CUtensorMap tm;
   const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, (uint32_t)(pl.tpc * 16));
@@ -409,6 +421,22 @@ static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
 }
 
 size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(8, M, N, K); }
+
+int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes, int64_t* fields,
+                 int nfields) {
+  if (!fields || nfields < 10) return QL_ERR_NULL_POINTER;
+  if ((wbits != 4 && wbits != 8) || M <= 0 || N <= 0 || K <= 0 || (wbits == 4 && K % 128 != 0))
+    return QL_ERR_BAD_SHAPE;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  const int sms = dev ? dev->sms : 148;   // without a device: the B200 SM count
+  GemvPlan pl;
+  if (!plan_gemv(wbits, M, N, K, sms, workspace_bytes, &pl)) return QL_ERR_UNSUPPORTED;
+  const int64_t v[10] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
+                         (int64_t)pl.nblk * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes};
+  for (int i = 0; i < 10; ++i) fields[i] = v[i];
+  return QL_OK;
+}
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }
 
 int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype, float* out, int64_t N, int64_t K,

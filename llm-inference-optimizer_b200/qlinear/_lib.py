@@ -52,6 +52,7 @@ SIGNATURES = {
                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
     "ql_w8a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_w4a16_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "ql_gemv_plan": (_int, [_int, _i64, _i64, _i64, _sz, ctypes.POINTER(_i64), _int]),
     "ql_w8a16_dequantize": (_int, [_vp, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "ql_w4a16_dequantize": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ql_w4a16_unpack": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
@@ -103,6 +104,18 @@ def check(status: int) -> None:
     if status != QL_OK:
         msg = load().ql_strerror(status)
         raise QLinearError(status, (msg or b"qlinear: error").decode())
+
+
+PLAN_FIELDS = ("tiles_per_cta", "warps_per_tile", "k_splits", "kblocks_per_split", "stages",
+               "batch_tiles", "batch_chunks", "ctas", "smem_bytes", "workspace_bytes")
+
+
+def gemv_plan(wbits: int, M: int, N: int, K: int, workspace_bytes: int | None = None) -> dict:
+    """The decode-kernel plan for a shape (see ql_gemv_plan)."""
+    buf = (_i64 * 10)()
+    avail = (1 << 64) - 1 if workspace_bytes is None else workspace_bytes
+    check(load().ql_gemv_plan(wbits, M, N, K, avail, buf, 10))
+    return dict(zip(PLAN_FIELDS, list(buf)))
 
 
 def version() -> tuple[int, int, int]:

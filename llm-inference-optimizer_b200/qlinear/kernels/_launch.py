@@ -45,6 +45,14 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def ld(t: torch.Tensor, row_len: int) -> int:
+    """Leading dimension (elements between rows) of a 2-D tensor with unit
+    inner stride.  A single-row tensor may report any row stride (torch
+    treats size-1 dims as contiguous whatever their stride), so its row
+    length is used instead."""
+    return t.stride(0) if t.shape[0] > 1 else row_len
+
+
 def dtype_code(dt: torch.dtype) -> int:
     if dt == torch.float16:
         return _lib.QL_DTYPE_F16

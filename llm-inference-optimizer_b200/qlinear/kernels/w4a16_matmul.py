@@ -22,7 +22,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ._launch import default_flags, dtype_code, on_device, ptr, workspace
+from ._launch import default_flags, dtype_code, ld, on_device, ptr, workspace
 
 GROUP_SIZE = 128
 HALF = GROUP_SIZE // 2
@@ -121,7 +121,7 @@ def w4a16_linear(
         status = lib.ql_w4a16_linear(
             ptr(x2), _lib.QL_DTYPE_F16, ptr(w_packed), layout, ptr(scales),
             ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
-            ptr(out), M, N, K, x2.stride(0), w_packed.stride(0), scales.stride(0), out.stride(0),
+            ptr(out), M, N, K, ld(x2, K), ld(w_packed, K // 2), ld(scales, N), ld(out, N),
             ptr(ws), ws.numel() if ws is not None else 0,
             default_flags(), stream.cuda_stream)
     _lib.check(status)

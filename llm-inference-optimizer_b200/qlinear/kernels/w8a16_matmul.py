@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ._launch import default_flags, dtype_code, on_device, ptr, workspace
+from ._launch import default_flags, dtype_code, ld, on_device, ptr, workspace
 
 
 def w8a16_linear(
@@ -70,7 +70,7 @@ def w8a16_linear(
             ptr(x2), _lib.QL_DTYPE_F16, ptr(w_q),
             ptr(scale), dtype_code(scale.dtype),
             ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
-            ptr(out), M, N, K, x2.stride(0), w_q.stride(0), out.stride(0),
+            ptr(out), M, N, K, ld(x2, K), ld(w_q, K), ld(out, N),
             ptr(ws), ws.numel() if ws is not None else 0,
             default_flags(), stream.cuda_stream)
     _lib.check(status)
