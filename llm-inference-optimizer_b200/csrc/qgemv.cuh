@@ -97,12 +97,144 @@ __device__ __forceinline__ float finish_value(const Params& p, float v, int n) {
   return v;
 }
 
+// B fragments (activations) of one 64-byte k-step for MT batch tiles: the
+// two 16-element runs of row t*8+g that this lane's weights multiply.  Rows
+// past the batch stay zero (their outputs are never stored).
+template <int MT>
+__device__ __forceinline__ void load_b(uint32_t (&b0)[MT][8], uint32_t (&b1)[MT][8], uint32_t xs_s,
+                                       int x_stride, int g, int mvalid, int e0, int e1) {
+  #pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
+    if (t * 8 + g < mvalid) {
+      const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * x_stride) * 2u;
+      v0 = lds128(xr + e0 * 2);
+      v1 = lds128(xr + e0 * 2 + 16);
+      v2 = lds128(xr + e1 * 2);
+      v3 = lds128(xr + e1 * 2 + 16);
+    }
+    b0[t][0] = v0.x; b0[t][1] = v0.y; b0[t][2] = v0.z; b0[t][3] = v0.w;
+    b0[t][4] = v1.x; b0[t][5] = v1.y; b0[t][6] = v1.z; b0[t][7] = v1.w;
+    b1[t][0] = v2.x; b1[t][1] = v2.y; b1[t][2] = v2.z; b1[t][3] = v2.w;
+    b1[t][4] = v3.x; b1[t][5] = v3.y; b1[t][6] = v3.z; b1[t][7] = v3.w;
+  }
+}
+
+// NS consecutive 64-byte k-steps (h0, h0+1, ...) of k-block `i` of one tile,
+// all loaded before any is computed so that their shared-memory loads and
+// mma chains overlap.  Every k-step keeps two independent accumulator
+// chains per batch tile.
+template <int WBITS, int LAYOUT, int MT, int NS>
+__device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t stage_s, int i, int h0, int rA, int rB,
+                                       int c, int g, uint32_t xs_s, int x_stride, int mvalid,
+                                       const float* ssc, int rows_cta) {
+  uint32_t wA[NS][4], wB[NS][4];
+  #pragma unroll
+  for (int n = 0; n < NS; ++n) {
+    const int q = (h0 + n) * 4 + c;
+    const uint4 a = lds128(stage_s + rA * kBlockBytes + ((q ^ (rA & 7)) << 4));
+    const uint4 b = lds128(stage_s + rB * kBlockBytes + ((q ^ (rB & 7)) << 4));
+    wA[n][0] = a.x; wA[n][1] = a.y; wA[n][2] = a.z; wA[n][3] = a.w;
+    wB[n][0] = b.x; wB[n][1] = b.y; wB[n][2] = b.z; wB[n][3] = b.w;
+  }
+  if (WBITS == 4) {
+    uint32_t bx0[NS][MT][8], bx1[NS][MT][8];
+    #pragma unroll
+    for (int n = 0; n < NS; ++n) {
+      const int kg = (i * 2 + h0 + n) * 128;     // first k of the group (relative to the split)
+      // split-half: low nibbles k = kg+16c.., high nibbles k = kg+64+16c..
+      // adjacent:   k = kg+32c .. kg+32c+31
+      const int e0 = LAYOUT == 0 ? kg + 16 * c : kg + 32 * c;
+      const int e1 = LAYOUT == 0 ? kg + 64 + 16 * c : kg + 32 * c + 16;
+      load_b<MT>(bx0[n], bx1[n], xs_s, x_stride, g, mvalid, e0, e1);
+    }
+    float part[NS][2][MT][4];
+    #pragma unroll
+    for (int n = 0; n < NS; ++n)
+      #pragma unroll
+      for (int u = 0; u < 2; ++u)
+        #pragma unroll
+        for (int t = 0; t < MT; ++t) part[n][u][t][0] = part[n][u][t][1] = part[n][u][t][2] = part[n][u][t][3] = 0.f;
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      #pragma unroll
+      for (int n = 0; n < NS; ++n) {
+        if (LAYOUT == 0) {
+          uint32_t al01, al23, ah01, ah23, bl01, bl23, bh01, bh23;
+          dec_w4_split(wA[n][j], al01, al23, ah01, ah23);
+          dec_w4_split(wB[n][j], bl01, bl23, bh01, bh23);
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            mma_16816(part[n][0][t], al01, bl01, al23, bl23, bx0[n][t][2 * j], bx0[n][t][2 * j + 1]);
+            mma_16816(part[n][1][t], ah01, bh01, ah23, bh23, bx1[n][t][2 * j], bx1[n][t][2 * j + 1]);
+          }
+        } else {
+          uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
+          dec_w4_adjacent(wA[n][j], a01, a23, a45, a67);
+          dec_w4_adjacent(wB[n][j], b01, b23, b45, b67);
+          const int jj = (j & 1) * 4;
+          #pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            const uint32_t* bx = j < 2 ? bx0[n][t] : bx1[n][t];
+            mma_16816(part[n][0][t], a01, b01, a23, b23, bx[jj], bx[jj + 1]);
+            mma_16816(part[n][1][t], a45, b45, a67, b67, bx[jj + 2], bx[jj + 3]);
+          }
+        }
+      }
+    }
+    #pragma unroll
+    for (int n = 0; n < NS; ++n) {
+      const int gl = i * 2 + h0 + n;
+      const float sA = ssc[gl * rows_cta + rA];
+      const float sB = ssc[gl * rows_cta + rB];
+      #pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        acc[n & 1][t][0] = fmaf(part[n][0][t][0] + part[n][1][t][0], sA, acc[n & 1][t][0]);
+        acc[n & 1][t][1] = fmaf(part[n][0][t][1] + part[n][1][t][1], sA, acc[n & 1][t][1]);
+        acc[n & 1][t][2] = fmaf(part[n][0][t][2] + part[n][1][t][2], sB, acc[n & 1][t][2]);
+        acc[n & 1][t][3] = fmaf(part[n][0][t][3] + part[n][1][t][3], sB, acc[n & 1][t][3]);
+      }
+    }
+  } else {
+    // int8: k = i*128 + (h0+n)*64 + 16c + 4j + {0..3}
+    uint32_t bx[NS][MT][8];
+    #pragma unroll
+    for (int n = 0; n < NS; ++n) {
+      const int e0 = i * kBlockBytes + (h0 + n) * 64 + 16 * c;
+      #pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+        if (t * 8 + g < mvalid) {
+          const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * x_stride) * 2u;
+          v0 = lds128(xr + e0 * 2);
+          v1 = lds128(xr + e0 * 2 + 16);
+        }
+        bx[n][t][0] = v0.x; bx[n][t][1] = v0.y; bx[n][t][2] = v0.z; bx[n][t][3] = v0.w;
+        bx[n][t][4] = v1.x; bx[n][t][5] = v1.y; bx[n][t][6] = v1.z; bx[n][t][7] = v1.w;
+      }
+    }
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      #pragma unroll
+      for (int n = 0; n < NS; ++n) {
+        uint32_t a01, a23, b01, b23;
+        dec_w8(wA[n][j], a01, a23);
+        dec_w8(wB[n][j], b01, b23);
+        #pragma unroll
+        for (int t = 0; t < MT; ++t)
+          mma_16816(acc[j & 1][t], a01, b01, a23, b23, bx[n][t][2 * j], bx[n][t][2 * j + 1]);
+      }
+    }
+  }
+}
+
 // MT = number of n8 batch tiles per CTA (mc = 8*MT batch rows per grid.z slice).
 template <int WBITS, int LAYOUT, int MT>
 __global__ void __launch_bounds__(kMaxThreads, 2)
     qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const Params p) {
   constexpr int MC = 8 * MT;
   constexpr int EPK = WBITS == 4 ? 256 : 128;      // k elements per k-block
+  constexpr int NS = MT == 1 ? 2 : 1;              // k-steps decoded together
   extern __shared__ uint8_t smem_raw[];
   // 128-byte-swizzled TMA destinations need 1024-byte aligned shared addresses
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -111,7 +243,8 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   const int ncw = tpc * wpt;                 // consumer warps
   const int nct = ncw * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_cta = tpc * kTileRows;
+  const int rows_cta = tpc * kTileRows;      // power of two
+  const int rows_log2 = 31 - __clz(rows_cta);
   const uint32_t box_bytes = static_cast<uint32_t>(rows_cta * kBlockBytes);
 
   const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, p.x_stride, p.kb_per_split);
@@ -141,7 +274,8 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   if (warp == ncw) {
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
-      const uint64_t pol = l2_policy_evict_first();
+      // weights are read once unless several batch chunks share them
+      const uint64_t pol = gridDim.z > 1 ? l2_policy_evict_last() : l2_policy_evict_first();
       if (!p.early_weights) griddep_wait();
       const int npre = min(stages, kbc);
       for (int i = 0; i < npre; ++i) {
@@ -163,19 +297,20 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
 
   // ----------------------------------------------------------- consumers
   const int ctid = threadIdx.x;
-  const int tt = warp / wpt, w = warp % wpt;
+  const int tt = warp / wpt, w = warp - tt * wpt;
   const int g = lane >> 2, c = lane & 3;
 
   // int4 group scales of this CTA's rows and groups -> fp32 in shared
-  // memory.  Scales are static like the weights, so this runs before the
-  // dependency wait.
+  // memory.  Scales are static like the weights, so they are loaded before
+  // the dependency wait (under programmatic dependent launch this overlaps
+  // the previous kernel).
   if (WBITS == 4) {
     const int G = p.K / 128;
     const int g0 = kb0 * 2;
     const int ng = min(kbc * 2, G - g0);
     const __half* sc = static_cast<const __half*>(p.scale);
-    for (int idx = ctid; idx < ng * rows_cta; idx += nct) {
-      const int gl = idx / rows_cta, r = idx - gl * rows_cta;
+    for (int idx = ctid; idx < (ng << rows_log2); idx += nct) {
+      const int gl = idx >> rows_log2, r = idx & (rows_cta - 1);
       const int n = row0 + r;
       ssc[idx] = n < p.N ? __half2float(sc[(long long)(g0 + gl) * p.lds + n]) : 0.f;
     }
@@ -189,20 +324,24 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   {
     const int kx0 = kb0 * EPK;
     const int nvec = kbc * EPK / 8;
-    for (int idx = ctid; idx < mvalid * nvec; idx += nct) {
-      const int mr = idx / nvec, v = idx - mr * nvec;
-      const int k = kx0 + v * 8;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (k < p.K) val = ldg_cg_v4(p.x + (long long)(m0 + mr) * p.ldx + k);
-      *reinterpret_cast<uint4*>(xs + mr * p.x_stride + v * 8) = val;
+    for (int mr = 0; mr < mvalid; ++mr) {
+      const __half* xrow = p.x + (long long)(m0 + mr) * p.ldx + kx0;
+      __half* srow = xs + mr * p.x_stride;
+      for (int v = ctid; v < nvec; v += nct) {
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (kx0 + v * 8 < p.K) val = ldg_cg_v4(xrow + v * 8);
+        *reinterpret_cast<uint4*>(srow + v * 8) = val;
+      }
     }
   }
   named_bar_sync(1, nct);
   griddep_launch_dependents();
 
-  float acc[MT][4];
+  float acc[2][MT][4];
   #pragma unroll
-  for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+  for (int u = 0; u < 2; ++u)
+    #pragma unroll
+    for (int t = 0; t < MT; ++t) acc[u][t][0] = acc[u][t][1] = acc[u][t][2] = acc[u][t][3] = 0.f;
 
   // mma row g <-> tile row prow: keeps the two rows a quarter-warp reads in
   // different 16-byte bank groups of the swizzled stage.
@@ -217,102 +356,16 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     const bool ok = mbar_wait(full + s, (i / stages) & 1, p.err, kDevErrFullWait);
     if (ok) {
       const uint32_t stage_s = ring_s + (uint32_t)s * box_bytes;
-      #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int byte_off = i * kBlockBytes + h * 64;
-        if (byte_off >= valid_bytes) break;
-        const int q = h * 4 + c;
-        const uint4 wa = lds128(stage_s + rA * kBlockBytes + ((q ^ (rA & 7)) << 4));
-        const uint4 wb = lds128(stage_s + rB * kBlockBytes + ((q ^ (rB & 7)) << 4));
-        const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
-        const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
-        if (WBITS == 4) {
-          const int gl = i * 2 + h;                 // group index within the split
-          const int kg = gl * 128;                  // its first k (relative to kx0)
-          // Activation offsets of the two 16-element runs this lane needs:
-          // split-half: low nibbles k = kg+16c.., high nibbles k = kg+64+16c..
-          // adjacent:   k = kg+32c .. kg+32c+31
-          const int e0 = LAYOUT == 0 ? kg + 16 * c : kg + 32 * c;
-          const int e1 = LAYOUT == 0 ? kg + 64 + 16 * c : kg + 32 * c + 16;
-          uint32_t bx0[MT][8], bx1[MT][8];
-          #pragma unroll
-          for (int t = 0; t < MT; ++t) {
-            uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
-            if (t * 8 + g < mvalid) {
-              const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * p.x_stride) * 2u;
-              v0 = lds128(xr + e0 * 2);
-              v1 = lds128(xr + e0 * 2 + 16);
-              v2 = lds128(xr + e1 * 2);
-              v3 = lds128(xr + e1 * 2 + 16);
-            }
-            bx0[t][0] = v0.x; bx0[t][1] = v0.y; bx0[t][2] = v0.z; bx0[t][3] = v0.w;
-            bx0[t][4] = v1.x; bx0[t][5] = v1.y; bx0[t][6] = v1.z; bx0[t][7] = v1.w;
-            bx1[t][0] = v2.x; bx1[t][1] = v2.y; bx1[t][2] = v2.z; bx1[t][3] = v2.w;
-            bx1[t][4] = v3.x; bx1[t][5] = v3.y; bx1[t][6] = v3.z; bx1[t][7] = v3.w;
-          }
-          float part[MT][4];
-          #pragma unroll
-          for (int t = 0; t < MT; ++t) part[t][0] = part[t][1] = part[t][2] = part[t][3] = 0.f;
-          #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (LAYOUT == 0) {
-              uint32_t al01, al23, ah01, ah23, bl01, bl23, bh01, bh23;
-              dec_w4_split(wA[j], al01, al23, ah01, ah23);
-              dec_w4_split(wB[j], bl01, bl23, bh01, bh23);
-              #pragma unroll
-              for (int t = 0; t < MT; ++t) {
-                // low nibbles: k = kg + 16c + 4j + {0..3}
-                mma_16816(part[t], al01, bl01, al23, bl23, bx0[t][2 * j], bx0[t][2 * j + 1]);
-                // high nibbles: k = kg + 64 + 16c + 4j + {0..3}
-                mma_16816(part[t], ah01, bh01, ah23, bh23, bx1[t][2 * j], bx1[t][2 * j + 1]);
-              }
-            } else {
-              uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
-              dec_w4_adjacent(wA[j], a01, a23, a45, a67);
-              dec_w4_adjacent(wB[j], b01, b23, b45, b67);
-              const int jj = (j & 1) * 4;
-              #pragma unroll
-              for (int t = 0; t < MT; ++t) {
-                // k = kg + 32c + 8j + {0..7}
-                const uint32_t* bx = j < 2 ? bx0[t] : bx1[t];
-                mma_16816(part[t], a01, b01, a23, b23, bx[jj], bx[jj + 1]);
-                mma_16816(part[t], a45, b45, a67, b67, bx[jj + 2], bx[jj + 3]);
-              }
-            }
-          }
-          const float sA = ssc[gl * rows_cta + rA];
-          const float sB = ssc[gl * rows_cta + rB];
-          #pragma unroll
-          for (int t = 0; t < MT; ++t) {
-            acc[t][0] = fmaf(part[t][0], sA, acc[t][0]);
-            acc[t][1] = fmaf(part[t][1], sA, acc[t][1]);
-            acc[t][2] = fmaf(part[t][2], sB, acc[t][2]);
-            acc[t][3] = fmaf(part[t][3], sB, acc[t][3]);
-          }
+      const int rem = valid_bytes - i * kBlockBytes;       // > 0
+      if (rem > 64) {
+        if (NS == 2) {
+          ksteps<WBITS, LAYOUT, MT, 2>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
         } else {
-          // int8: k = byte_off + 16c + 4j + {0..3}
-          const int e0 = byte_off + 16 * c;
-          uint32_t bx[MT][8];
-          #pragma unroll
-          for (int t = 0; t < MT; ++t) {
-            uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
-            if (t * 8 + g < mvalid) {
-              const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * p.x_stride) * 2u;
-              v0 = lds128(xr + e0 * 2);
-              v1 = lds128(xr + e0 * 2 + 16);
-            }
-            bx[t][0] = v0.x; bx[t][1] = v0.y; bx[t][2] = v0.z; bx[t][3] = v0.w;
-            bx[t][4] = v1.x; bx[t][5] = v1.y; bx[t][6] = v1.z; bx[t][7] = v1.w;
-          }
-          #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t a01, a23, b01, b23;
-            dec_w8(wA[j], a01, a23);
-            dec_w8(wB[j], b01, b23);
-            #pragma unroll
-            for (int t = 0; t < MT; ++t) mma_16816(acc[t], a01, b01, a23, b23, bx[t][2 * j], bx[t][2 * j + 1]);
-          }
+          ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
+          ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 1, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
         }
+      } else {
+        ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
       }
     }
     __syncwarp();
@@ -327,38 +380,38 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     #pragma unroll
     for (int t = 0; t < MT; ++t) {
       const int mm = t * 8 + 2 * c;
-      mine[(mm + 0) * kTileRows + prow] = acc[t][0];
-      mine[(mm + 1) * kTileRows + prow] = acc[t][1];
-      mine[(mm + 0) * kTileRows + prow + 8] = acc[t][2];
-      mine[(mm + 1) * kTileRows + prow + 8] = acc[t][3];
+      mine[(mm + 0) * kTileRows + prow] = acc[0][t][0] + acc[1][t][0];
+      mine[(mm + 1) * kTileRows + prow] = acc[0][t][1] + acc[1][t][1];
+      mine[(mm + 0) * kTileRows + prow + 8] = acc[0][t][2] + acc[1][t][2];
+      mine[(mm + 1) * kTileRows + prow + 8] = acc[0][t][3] + acc[1][t][3];
     }
   }
   named_bar_sync(1, nct);
 
-  const int nout = MC * rows_cta;   // (m, r) pairs of this CTA, r fastest
+  const int nout = mvalid << rows_log2;   // (m, r) pairs of this CTA, r fastest
   if (p.ks == 1) {
     for (int idx = ctid; idx < nout; idx += nct) {
-      const int m = idx / rows_cta, r = idx - m * rows_cta;
+      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
       const int t = r >> 4, rr = r & 15;
       float v = 0.f;
-      for (int w2 = 0; w2 < wpt; ++w2) v += red[((size_t)(t * wpt + w2) * MC + m) * kTileRows + rr];
-      const int n = row0 + r, mm = m0 + m;
-      if (n < p.N && mm < p.M) p.out[(long long)mm * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+      for (int w2 = 0; w2 < wpt; ++w2) v += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
+      const int n = row0 + r;
+      if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
     }
     return;
   }
 
   // ----------------------------------------- cross-CTA split-K reduction
-  const size_t slot_elems = (size_t)MC * rows_cta;
+  const int slot_elems = MC << rows_log2;
   const size_t tile_id = (size_t)mchunk * gridDim.x + blk;
   float* slots = p.partials + tile_id * p.ks * slot_elems;
   {
     float* mine = slots + (size_t)split * slot_elems;
     for (int idx = ctid; idx < nout; idx += nct) {
-      const int m = idx / rows_cta, r = idx - m * rows_cta;
+      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
       const int t = r >> 4, rr = r & 15;
       float v = 0.f;
-      for (int w2 = 0; w2 < wpt; ++w2) v += red[((size_t)(t * wpt + w2) * MC + m) * kTileRows + rr];
+      for (int w2 = 0; w2 < wpt; ++w2) v += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
       mine[idx] = v;
     }
   }
@@ -378,9 +431,9 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
         v += __ldcg(slot);
         __stcg(slot, 0.f);                       // leave the workspace zeroed
       }
-      const int m = idx / rows_cta, r = idx - m * rows_cta;
-      const int n = row0 + r, mm = m0 + m;
-      if (n < p.N && mm < p.M) p.out[(long long)mm * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
+      const int n = row0 + r;
+      if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
     }
     if (ctid == 0) p.counters[tile_id] = 0u;     // leave the workspace zeroed
   }
