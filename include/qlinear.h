@@ -129,9 +129,10 @@ size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
 
 /* The decode-kernel plan the library would use for (wbits, M, N, K) with a
  * workspace of `workspace_bytes` (SIZE_MAX = unlimited), for tuning and
- * tests.  fields[0..9] = tiles of 16 rows per CTA, consumer warps per tile,
+ * tests.  fields[0..11] = tiles of 16 rows per CTA, consumer warps per tile,
  * K-splits, 128-byte k-blocks per split, ring stages, batch tiles of 8 per
- * CTA, batch chunks, CTAs, dynamic shared bytes, workspace bytes.  Has no
+ * CTA, batch chunks, CTAs, dynamic shared bytes, workspace bytes, k-blocks
+ * per stage, bytes of the innermost tensor-map dimension (nfields >= 12).  Has no
  * counterpart in the reference (its Triton configs are fixed in
  * _pick_config, w8a16_matmul_triton.py:89-99). */
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes,

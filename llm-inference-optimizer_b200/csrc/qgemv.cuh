@@ -8,24 +8,29 @@
 //   * A "tile" is 16 consecutive weight rows (output columns n).  A CTA owns
 //     `tpc` consecutive tiles and one K-split of `kb_per_split` k-blocks; a
 //     k-block is 128 bytes of every row (256 k for int4, 128 k for int8).
-//   * One producer thread streams the CTA's weight slice through a ring of
-//     `stages` shared-memory slots with 2-D TMA (box = tpc*16 rows x 128 B,
-//     128-byte swizzle), completion on mbarriers.  With programmatic
-//     dependent launch the whole prologue of that stream is issued before
-//     the kernel waits for its predecessor: weights do not depend on it.
-//   * Consumer warps: `wpt` warps per tile, each taking every wpt-th k-block.
-//     A warp reads two 16-byte chunks per 64-byte k-step (rows g and g+8 of
-//     its tile), decodes them in registers to exact fp16 integers, and
-//     issues mma.sync m16n8k16 with the weights as the 16-row A operand and
-//     the activations (x slice staged in shared memory) as the n8 operand
-//     ("swap-AB": the batch is the narrow side).  fp32 accumulation; the
-//     int4 group scale is applied to each 128-k group partial in fp32, the
-//     int8 row scale once at the end — as in the reference kernels.
+//   * Weights stream through shared memory in stages of one tile x
+//     `kb_stage` k-blocks.  Each stage is ONE 3-D TMA box over the rows
+//     viewed as [N][kbytes/C][C] (C = 128, 64, 32 or 16 bytes), so every
+//     request covers 16 runs of kb_stage*128 contiguous bytes — whole rows
+//     when the split spans K — which keeps HBM pages streaming.  Boxes past
+//     the row end read as zero.  One producer thread issues all stages that
+//     fit up front; with programmatic dependent launch that happens before
+//     the kernel waits for its predecessor (weights do not depend on it).
+//   * Consumer warps: `wpt` warps per tile split each stage's k-blocks.  A
+//     warp loads 16-byte chunks of rows g and g+8, decodes them in registers
+//     to exact fp16 integers and issues mma.sync m16n8k16 with the weights
+//     as the 16-row A operand and the activations (x slice staged in shared
+//     memory) as the n8 operand ("swap-AB": the batch is the narrow side).
+//     Odd rows load the two 64-byte halves of a k-block in the opposite
+//     order to even rows, so each quarter-warp touches all 32 banks once.
+//     fp32 accumulation; the int4 group scale multiplies each 128-k group
+//     partial in fp32, the int8 row scale multiplies the sum once at the
+//     end — as in the reference kernels.
 //   * Warps of a tile reduce through shared memory in a fixed order.  With
 //     more than one K-split, each CTA writes an fp32 partial to its own
 //     workspace slot and the last CTA to arrive (atomic counter) sums the
-//     slots in slot order, applies scale/bias and resets the counter, so the
-//     result is deterministic and the workspace stays zeroed.
+//     slots in slot order, applies scale/bias and zeroes slots and counter,
+//     so the result is deterministic and the workspace stays zeroed.
 #pragma once
 
 #include "ql_common.cuh"
@@ -34,7 +39,7 @@ namespace ql {
 namespace gemv {
 
 constexpr int kTileRows = 16;
-constexpr int kBlockBytes = 128;    // k-block width = TMA box inner extent (SW128)
+constexpr int kBlockBytes = 128;    // k-block width
 // At most 8 consumer warps + 1 producer warp, so that two CTAs fit on an SM
 // by registers: the next kernel's CTAs can then start streaming their
 // weights (programmatic dependent launch) while this kernel finishes.
@@ -54,7 +59,9 @@ struct Params {
   int ks;                 // number of K-splits (gridDim.y)
   int tpc;                // tiles per CTA
   int wpt;                // consumer warps per tile
-  int stages;             // ring depth
+  int kb_stage;           // k-blocks per stage (divides kb_per_split or covers it)
+  int stages;             // ring depth (stages resident at once)
+  int chunk;              // C: bytes of the innermost tensor-map dimension
   int x_stride;           // halves per staged x row
   int x_rows;             // staged x rows = min(8*MT, M)
   int scale_f32;          // int8 scale dtype
@@ -70,16 +77,16 @@ struct Smem {
   size_t ring, red, region0, x, sc, bars, total;
 };
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-__host__ __device__ inline Smem smem_layout(int wbits, int mc, int x_rows, int tpc, int wpt,
-                                            int stages, int x_stride, int kb_per_split) {
+__host__ __device__ inline Smem smem_layout(int wbits, int mc, int x_rows, int tpc, int wpt, int stages,
+                                            int kb_stage, int x_stride, int kb_per_split) {
   Smem s;
-  s.ring = (size_t)stages * tpc * kTileRows * kBlockBytes;
+  s.ring = (size_t)stages * kTileRows * kb_stage * kBlockBytes;
   s.red = (size_t)tpc * wpt * kTileRows * mc * 4;
-  s.region0 = align_up(s.ring > s.red ? s.ring : s.red, 1024);
+  s.region0 = align_up(s.ring > s.red ? s.ring : s.red, 128);
   s.x = align_up((size_t)x_rows * x_stride * 2, 16);
   s.sc = wbits == 4 ? align_up((size_t)kb_per_split * 2 * tpc * kTileRows * 4, 16) : 0;
   s.bars = align_up((size_t)2 * stages * 8 + 16, 16);
-  s.total = 1024 /* base alignment slack */ + s.region0 + s.x + s.sc + s.bars;
+  s.total = 128 /* base alignment slack */ + s.region0 + s.x + s.sc + s.bars;
   return s;
 }
 
@@ -120,22 +127,35 @@ __device__ __forceinline__ void load_b(uint32_t (&b0)[MT][8], uint32_t (&b1)[MT]
   }
 }
 
+__device__ __forceinline__ void u4_to_words(const uint4& v, uint32_t (&w)[4]) {
+  w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+}
+
 // NS consecutive 64-byte k-steps (h0, h0+1, ...) of k-block `i` of one tile,
 // all loaded before any is computed so that their shared-memory loads and
 // mma chains overlap.  Every k-step keeps two independent accumulator
-// chains per batch tile.
+// chains per batch tile.  `rowA`/`rowB` are the shared addresses of this
+// k-block's 128 bytes in rows g and g+8; `odd` = g & 1.
 template <int WBITS, int LAYOUT, int MT, int NS>
-__device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t stage_s, int i, int h0, int rA, int rB,
-                                       int c, int g, uint32_t xs_s, int x_stride, int mvalid,
-                                       const float* ssc, int rows_cta) {
+__device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, uint32_t rowB, int i, int h0,
+                                       int c, int g, bool odd, uint32_t xs_s, int x_stride, int mvalid,
+                                       const float* scA, const float* scB, int sc_stride) {
   uint32_t wA[NS][4], wB[NS][4];
-  #pragma unroll
-  for (int n = 0; n < NS; ++n) {
-    const int q = (h0 + n) * 4 + c;
-    const uint4 a = lds128(stage_s + rA * kBlockBytes + ((q ^ (rA & 7)) << 4));
-    const uint4 b = lds128(stage_s + rB * kBlockBytes + ((q ^ (rB & 7)) << 4));
-    wA[n][0] = a.x; wA[n][1] = a.y; wA[n][2] = a.z; wA[n][3] = a.w;
-    wB[n][0] = b.x; wB[n][1] = b.y; wB[n][2] = b.z; wB[n][3] = b.w;
+  if (NS == 2) {
+    // even rows read half 0 then 1, odd rows half 1 then 0: a quarter-warp
+    // (two rows x four chunks) then covers all eight 16-byte bank groups
+    const uint32_t c0 = (uint32_t)(((odd ? 1 : 0) * 4 + c) << 4);
+    const uint32_t c1 = (uint32_t)(((odd ? 0 : 1) * 4 + c) << 4);
+    const uint4 a0 = lds128(rowA + c0), a1 = lds128(rowA + c1);
+    const uint4 b0 = lds128(rowB + c0), b1 = lds128(rowB + c1);
+    u4_to_words(odd ? a1 : a0, wA[0]);
+    u4_to_words(odd ? a0 : a1, wA[NS - 1]);
+    u4_to_words(odd ? b1 : b0, wB[0]);
+    u4_to_words(odd ? b0 : b1, wB[NS - 1]);
+  } else {
+    const uint32_t co = (uint32_t)((h0 * 4 + c) << 4);
+    u4_to_words(lds128(rowA + co), wA[0]);
+    u4_to_words(lds128(rowB + co), wB[0]);
   }
   if (WBITS == 4) {
     uint32_t bx0[NS][MT][8], bx1[NS][MT][8];
@@ -185,8 +205,8 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t stage_s,
     #pragma unroll
     for (int n = 0; n < NS; ++n) {
       const int gl = i * 2 + h0 + n;
-      const float sA = ssc[gl * rows_cta + rA];
-      const float sB = ssc[gl * rows_cta + rB];
+      const float sA = scA[gl * sc_stride];
+      const float sB = scB[gl * sc_stride];
       #pragma unroll
       for (int t = 0; t < MT; ++t) {
         acc[n & 1][t][0] = fmaf(part[n][0][t][0] + part[n][1][t][0], sA, acc[n & 1][t][0]);
@@ -236,18 +256,17 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   constexpr int EPK = WBITS == 4 ? 256 : 128;      // k elements per k-block
   constexpr int NS = MT == 1 ? 2 : 1;              // k-steps decoded together
   extern __shared__ uint8_t smem_raw[];
-  // 128-byte-swizzled TMA destinations need 1024-byte aligned shared addresses
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
 
-  const int tpc = p.tpc, wpt = p.wpt, stages = p.stages;
+  const int tpc = p.tpc, wpt = p.wpt, stages = p.stages, kb_stage = p.kb_stage;
   const int ncw = tpc * wpt;                 // consumer warps
   const int nct = ncw * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_cta = tpc * kTileRows;      // power of two
   const int rows_log2 = 31 - __clz(rows_cta);
-  const uint32_t box_bytes = static_cast<uint32_t>(rows_cta * kBlockBytes);
+  const uint32_t stage_bytes = static_cast<uint32_t>(kTileRows * kb_stage * kBlockBytes);
 
-  const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, p.x_stride, p.kb_per_split);
+  const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, kb_stage, p.x_stride, p.kb_per_split);
   uint8_t* ring = smem;
   __half* xs = reinterpret_cast<__half*>(smem + L.region0);
   float* ssc = reinterpret_cast<float*>(smem + L.region0 + L.x);
@@ -259,37 +278,35 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   const int row0 = blk * rows_cta;
   const int kb0 = split * p.kb_per_split;
   const int kbc = min(p.kb_per_split, p.nkb - kb0);
+  const int nkc = (kbc + kb_stage - 1) / kb_stage;   // k-chunks (stages per tile)
   const int m0 = mchunk * MC;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, tpc);
+      mbar_init(empty + s, wpt);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
   // ------------------------------------------------------------ producer
+  // Stage st = kc * tpc + tt holds tile tt, k-blocks [kc*kb_stage, +kb_stage).
   if (warp == ncw) {
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
       // weights are read once unless several batch chunks share them
       const uint64_t pol = gridDim.z > 1 ? l2_policy_evict_last() : l2_policy_evict_first();
       if (!p.early_weights) griddep_wait();
-      const int npre = min(stages, kbc);
-      for (int i = 0; i < npre; ++i) {
-        mbar_arrive_expect_tx(full + i, box_bytes);
-        tma_load_2d(smem_u32(ring + (size_t)i * box_bytes), &tmap_w, (kb0 + i) * kBlockBytes, row0,
-                    full + i, pol);
-      }
-      for (int i = stages; i < kbc; ++i) {
-        const int s = i % stages;
-        const uint32_t par = ((i / stages) - 1) & 1;
-        mbar_wait(empty + s, par, p.err, kDevErrEmptyWait);   // on timeout: error recorded, go on
-        mbar_arrive_expect_tx(full + s, box_bytes);
-        tma_load_2d(smem_u32(ring + (size_t)s * box_bytes), &tmap_w, (kb0 + i) * kBlockBytes, row0,
-                    full + s, pol);
+      const int per_kb = kBlockBytes / p.chunk;
+      const int total = nkc * tpc;
+      for (int st = 0; st < total; ++st) {
+        const int s = st % stages;
+        if (st >= stages) mbar_wait(empty + s, ((st / stages) - 1) & 1, p.err, kDevErrEmptyWait);
+        const int kc = st / tpc, tt = st - kc * tpc;
+        mbar_arrive_expect_tx(full + s, stage_bytes);
+        tma_load_3d(smem_u32(ring + (size_t)s * stage_bytes), &tmap_w, 0, (kb0 + kc * kb_stage) * per_kb,
+                    row0 + tt * kTileRows, full + s, pol);
       }
     }
     return;
@@ -343,29 +360,42 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     #pragma unroll
     for (int t = 0; t < MT; ++t) acc[u][t][0] = acc[u][t][1] = acc[u][t][2] = acc[u][t][3] = 0.f;
 
-  // mma row g <-> tile row prow: keeps the two rows a quarter-warp reads in
-  // different 16-byte bank groups of the swizzled stage.
-  const int prow = (g >> 1) | ((g & 1) << 2);
-  const int rA = tt * kTileRows + prow, rB = rA + 8;
   const uint32_t ring_s = smem_u32(ring);
   const uint32_t xs_s = smem_u32(xs);
   const int valid_bytes = p.kbytes - kb0 * kBlockBytes;
+  const bool odd = (g & 1) != 0;
+  const float* scA = ssc + tt * kTileRows + g;      // scale of row g of this tile, group 0
+  const float* scB = scA + 8;
+  const uint32_t rowA_off = (uint32_t)(g * kb_stage * kBlockBytes);
+  const uint32_t rowB_off = (uint32_t)((g + 8) * kb_stage * kBlockBytes);
 
-  for (int i = w; i < kbc; i += wpt) {
-    const int s = i % stages;
-    const bool ok = mbar_wait(full + s, (i / stages) & 1, p.err, kDevErrFullWait);
+  for (int kc = 0; kc < nkc; ++kc) {
+    const int st = kc * tpc + tt;
+    const int s = st % stages;
+    const bool ok = mbar_wait(full + s, (st / stages) & 1, p.err, kDevErrFullWait);
     if (ok) {
-      const uint32_t stage_s = ring_s + (uint32_t)s * box_bytes;
-      const int rem = valid_bytes - i * kBlockBytes;       // > 0
-      if (rem > 64) {
-        if (NS == 2) {
-          ksteps<WBITS, LAYOUT, MT, 2>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
+      const uint32_t tile_s = ring_s + (uint32_t)s * stage_bytes;
+      const int kb_lo = kc * kb_stage;
+      const int kb_hi = min(kb_stage, kbc - kb_lo);
+      for (int kbl = w; kbl < kb_hi; kbl += wpt) {
+        const int i = kb_lo + kbl;                          // k-block within the split
+        const uint32_t rowA = tile_s + rowA_off + (uint32_t)(kbl * kBlockBytes);
+        const uint32_t rowB = tile_s + rowB_off + (uint32_t)(kbl * kBlockBytes);
+        const int rem = valid_bytes - i * kBlockBytes;       // > 0
+        if (rem > 64) {
+          if (NS == 2) {
+            ksteps<WBITS, LAYOUT, MT, 2>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
+                                         rows_cta);
+          } else {
+            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
+                                         rows_cta);
+            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 1, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
+                                         rows_cta);
+          }
         } else {
-          ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
-          ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 1, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
+          ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
+                                       rows_cta);
         }
-      } else {
-        ksteps<WBITS, LAYOUT, MT, 1>(acc, stage_s, i, 0, rA, rB, c, g, xs_s, p.x_stride, mvalid, ssc, rows_cta);
       }
     }
     __syncwarp();
@@ -380,10 +410,10 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     #pragma unroll
     for (int t = 0; t < MT; ++t) {
       const int mm = t * 8 + 2 * c;
-      mine[(mm + 0) * kTileRows + prow] = acc[0][t][0] + acc[1][t][0];
-      mine[(mm + 1) * kTileRows + prow] = acc[0][t][1] + acc[1][t][1];
-      mine[(mm + 0) * kTileRows + prow + 8] = acc[0][t][2] + acc[1][t][2];
-      mine[(mm + 1) * kTileRows + prow + 8] = acc[0][t][3] + acc[1][t][3];
+      mine[(mm + 0) * kTileRows + g] = acc[0][t][0] + acc[1][t][0];
+      mine[(mm + 1) * kTileRows + g] = acc[0][t][1] + acc[1][t][1];
+      mine[(mm + 0) * kTileRows + g + 8] = acc[0][t][2] + acc[1][t][2];
+      mine[(mm + 1) * kTileRows + g + 8] = acc[0][t][3] + acc[1][t][3];
     }
   }
   named_bar_sync(1, nct);

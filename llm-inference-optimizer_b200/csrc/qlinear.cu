@@ -88,17 +88,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D uint8 map over rows of `inner_bytes` valid bytes, 128-byte swizzle.
-int make_weight_map(CUtensorMap* tm, const void* base, uint64_t inner_bytes, uint64_t rows,
-                    uint64_t row_stride, uint32_t box_rows) {
+// Weight rows viewed as a 3-D uint8 tensor [rows][kbytes/C][C]: a box of
+// (C, kb_stage*128/C, 16) is 16 runs of kb_stage*128 contiguous bytes.
+// C is the largest of 128/64/32/16 dividing the row length, so the middle
+// dimension ends exactly at the row end and anything past it reads as zero.
+int weight_chunk(uint64_t kbytes) {
+  for (int c : {128, 64, 32, 16})
+    if (kbytes % c == 0) return c;
+  return 0;
+}
+
+int make_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uint64_t rows, uint64_t row_stride,
+                    int chunk, int kb_stage) {
   auto fn = encode_fn();
   if (!fn) return QL_ERR_DEVICE;
-  cuuint64_t dims[2] = {inner_bytes, rows};
-  cuuint64_t strides[1] = {row_stride};
-  cuuint32_t box[2] = {128, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  cuuint64_t dims[3] = {(cuuint64_t)chunk, kbytes / chunk, rows};
+  cuuint64_t strides[2] = {(cuuint64_t)chunk, row_stride};
+  cuuint32_t box[3] = {(cuuint32_t)chunk, (cuuint32_t)(kb_stage * 128 / chunk), 16};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
 }
@@ -145,7 +154,7 @@ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // ------------------------------------------------------------- GEMV plan
 struct GemvPlan {
-  int tpc = 0, wpt = 0, ks = 0, kbps = 0, stages = 0, mt = 0, mchunks = 0;
+  int tpc = 0, wpt = 0, ks = 0, kbps = 0, stages = 0, kb_stage = 0, chunk = 0, mt = 0, mchunks = 0;
   int x_stride = 0, x_rows = 0, nblk = 0, nkb = 0;
   size_t smem = 0, ws_bytes = 0, ws_counters = 0;
   double cost = 0;
@@ -222,16 +231,34 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
       p.ws_bytes = gemv_ws_bytes(p);
       if (p.ws_bytes > ws_avail) continue;
-      // ring depth: the whole slice if it fits next to a second CTA, else
-      // as many stages as fit at all
-      const size_t box = (size_t)tpc * 16 * 128;
-      const ql::gemv::Smem base = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, p.x_stride, kbps);
-      const size_t fixed = base.total - base.region0 + 2 * 8 * 32;
-      int fit = kSmemShared > fixed ? (int)std::min<size_t>(32, (kSmemShared - fixed) / box) : 0;
-      if (fit < std::min(kbps, 2)) fit = (int)std::min<size_t>(32, (kSmemOptin - fixed) / box);
-      p.stages = std::min(kbps, fit);
-      if (p.stages < std::min(kbps, 2)) continue;
-      p.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, p.stages, p.x_stride, kbps).total;
+      // stages of one tile x kb_stage k-blocks: the whole slice resident if
+      // it fits next to a second CTA; else the fewest k-chunks that still
+      // double-buffer every tile; else whatever fits at all
+      const int chunk = weight_chunk((uint64_t)kbytes);
+      if (chunk == 0) continue;
+      const ql::gemv::Smem base =
+          ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, 1, p.x_stride, kbps);
+      const size_t fixed = base.total - base.region0 + 2 * 8 * 64;
+      bool placed = false;
+      for (size_t budget : {kSmemShared, kSmemOptin}) {
+        if (budget <= fixed) continue;
+        for (int nkc = 1; nkc <= kbps && !placed; ++nkc) {
+          const int kbs = (int)cdiv(kbps, nkc);
+          if (kbs * 128 / chunk > 256) continue;
+          const size_t stage_bytes = (size_t)16 * kbs * 128;
+          const int fit = (int)std::min<size_t>(64, (budget - fixed) / stage_bytes);
+          const int total = tpc * nkc;
+          if (fit >= total || (nkc > 1 && fit >= 2 * tpc) || (nkc == kbps && fit >= 1)) {
+            p.kb_stage = kbs;
+            p.stages = std::min(fit, total);
+            placed = true;
+          }
+        }
+        if (placed) break;
+      }
+      if (!placed) continue;
+      p.chunk = chunk;
+      p.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, p.stages, p.kb_stage, p.x_stride, kbps).total;
       if (p.smem > kSmemOptin) continue;
       const double ctas = (double)nblk * ks_eff * mchunks;
       const double waves = std::ceil(ctas / sms);
@@ -312,7 +339,7 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return run_generic(a);
   CUtensorMap tm;
   const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
-  int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, (uint32_t)(pl.tpc * 16));
+  int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, pl.chunk, pl.kb_stage);
   if (st != QL_OK) return st;
   ql::gemv::Params p;
   p.x = static_cast<const __half*>(a.x);
@@ -332,6 +359,8 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   p.tpc = pl.tpc;
   p.wpt = pl.wpt;
   p.stages = pl.stages;
+  p.kb_stage = pl.kb_stage;
+  p.chunk = pl.chunk;
   p.x_stride = pl.x_stride;
   p.x_rows = pl.x_rows;
   p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
@@ -424,7 +453,7 @@ size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspa
 
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes, int64_t* fields,
                  int nfields) {
-  if (!fields || nfields < 10) return QL_ERR_NULL_POINTER;
+  if (!fields || nfields < 12) return QL_ERR_NULL_POINTER;
   if ((wbits != 4 && wbits != 8) || M <= 0 || N <= 0 || K <= 0 || (wbits == 4 && K % 128 != 0))
     return QL_ERR_BAD_SHAPE;
   int st;
@@ -432,9 +461,10 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
   const int sms = dev ? dev->sms : 148;   // without a device: the B200 SM count
   GemvPlan pl;
   if (!plan_gemv(wbits, M, N, K, sms, workspace_bytes, &pl)) return QL_ERR_UNSUPPORTED;
-  const int64_t v[10] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
-                         (int64_t)pl.nblk * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes};
-  for (int i = 0; i < 10; ++i) fields[i] = v[i];
+  const int64_t v[12] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
+                         (int64_t)pl.nblk * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes,
+                         pl.kb_stage, pl.chunk};
+  for (int i = 0; i < 12; ++i) fields[i] = v[i];
   return QL_OK;
 }
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }
