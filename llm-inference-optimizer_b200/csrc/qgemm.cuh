@@ -1,0 +1,320 @@
+// qgemm.cuh — prefill-shaped (larger M) dequant-fused GEMM on the 5th-gen
+// tensor cores (tcgen05 / TMEM).
+//
+// Replaces the reference's Triton kernels for large M
+// (_w8a16_matmul_kernel, src/kernels/w8a16_matmul_triton.py:39-86;
+//  _w4a16_matmul_kernel, src/kernels/w4a16_matmul_triton.py:62-117).
+//
+// "Swap-AB" formulation: D[n, m] = sum_k W[n, k] * x[m, k], so the
+// dequantized weights are the MMA's A operand (M = 128 weight rows per CTA)
+// and the activations are the B operand (N = BN activation rows per CTA).
+//   * warp 0 (one thread): TMA producer.  Per 128-k stage it loads the
+//     packed weight tile (128 rows x 64 B int4 / 128 B int8, 64/128-byte
+//     swizzle, a 3-D view of the rows) and the activation tile (BN rows x
+//     128 k as two 128-byte-swizzled K-major atoms).
+//   * warps 2-5 (128 threads, thread = weight row = TMEM lane): read their
+//     row's packed bytes, decode them to fp16 in registers (int4: times
+//     the fp16 group scale, one rounding per weight; int8: exact) and write
+//     them into TMEM with tcgen05.st — the A operand never touches shared
+//     memory, which keeps shared-memory bandwidth for the activations.
+//   * warp 1 (one thread): issues tcgen05.mma.cta_group::1.kind::f16
+//     (A from TMEM, B from shared memory by descriptor, fp32 accumulator
+//     in TMEM) and tcgen05.commit's the stage back to producer/dequant.
+//   * epilogue (warps 2-5): tcgen05.ld of the accumulator, int8 row scale
+//     and bias in fp32, fp16 store (32 consecutive n per warp per row).
+// No cluster multicast anywhere; every wait is bounded.
+#pragma once
+
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gemm {
+
+constexpr int kTileN = 128;     // weight rows per CTA = UMMA M
+constexpr int kBK = 128;        // k per stage = 8 MMAs of K=16
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kASlots = 2;      // A (dequantized weight) stages in TMEM
+
+struct Params {
+  const void* scale;      // int8: [N] f32/f16; int4: [K/128, lds] f16
+  const void* bias;       // [N] or nullptr
+  __half* out;            // [M, ldo]
+  long long lds, ldo;
+  int M, N, K;
+  int nk;                 // number of 128-k stages
+  int stages;             // shared-memory ring depth
+  int scale_f32, bias_f32;
+  unsigned* err;
+};
+
+template <int WBITS, int BN>
+struct Layout {
+  static constexpr int kWStage = kTileN * (WBITS == 4 ? 64 : 128);
+  static constexpr int kXAtom = BN * 128;           // 64 k x BN rows of fp16
+  static constexpr int kXStage = 2 * kXAtom;
+  static constexpr int kStage = kXStage + kWStage;  // multiple of 1024
+  static constexpr uint32_t kTmemCols = BN + kASlots * 64 <= 256 ? 256 : 512;
+  static constexpr uint32_t kACol = BN <= 128 ? 128 : 256;  // first A column
+  static constexpr uint32_t kTx = kStage;
+  static size_t smem_bytes(int stages) { return 1024 + (size_t)stages * kStage + 256; }
+};
+
+// ----------------------------------------------------------- tcgen05 ops
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, fp32 accumulate
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: kind::f16, A/B fp16, fp32 accumulator, both
+// K-major, M = 128, N = BN.
+template <int BN>
+__device__ __forceinline__ uint32_t idesc_f16() {
+  return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTileN >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+template <int WBITS, int LAYOUT, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                 const Params p) {
+  using L = Layout<WBITS, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * L::kStage);
+  uint64_t* wfree = full + S;
+  uint64_t* xfree = wfree + S;
+  uint64_t* afull = xfree + S;
+  uint64_t* afree = afull + kASlots;
+  uint64_t* dfull = afree + kASlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTileN;
+  const int m0 = blockIdx.y * BN;
+  const int nk = p.nk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(wfree + s, 4);
+      mbar_init(xfree + s, 1);
+    }
+    for (int a = 0; a < kASlots; ++a) {
+      mbar_init(afull + a, 4);
+      mbar_init(afree + a, 1);
+    }
+    mbar_init(dfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      prefetch_tmap(&tmap_w);
+      const uint64_t pol_w = l2_policy_evict_last();   // reused by every activation tile
+      const uint64_t pol_x = l2_policy_evict_last();   // reused by every weight tile
+      griddep_wait();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S;
+        if (i >= S) {
+          const uint32_t par = ((i / S) - 1) & 1;
+          mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait);
+          mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait);
+        }
+        uint8_t* st = smem + (size_t)s * L::kStage;
+        mbar_arrive_expect_tx(full + s, L::kTx);
+        tma_load_2d(smem_u32(st), &tmap_x, i * kBK, m0, full + s, pol_x);
+        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, i * kBK + 64, m0, full + s, pol_x);
+        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, i, n0, full + s, pol_w);
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16<BN>();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S, a = i % kASlots;
+        mbar_wait(full + s, (i / S) & 1, p.err, kDevErrMmaWait);
+        mbar_wait(afull + a, (i / kASlots) & 1, p.err, kDevErrMmaWait);
+        tc_fence_after();
+        const uint32_t xs = smem_u32(smem + (size_t)s * L::kStage);
+        const uint32_t a_tmem = tmem + L::kACol + 64u * a;
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint64_t bd = desc_sw128(xs + (uint32_t)((j >> 2) * L::kXAtom + (j & 3) * 32));
+          tc_mma_ts(tmem, a_tmem + 8u * j, bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+        }
+        tc_commit(xfree + s);
+        tc_commit(afree + a);
+      }
+      tc_commit(dfull);
+    }
+  } else {
+    // ------------------------------------------------ dequant + epilogue
+    const int quarter = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;            // weight row within the tile = TMEM lane
+    const int n = n0 + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const __half* sc4 = static_cast<const __half*>(p.scale);
+    // int4 group scale of this row for stage i (0 past N), two stages ahead
+    auto load_scale = [&](int i) -> __half {
+      return (WBITS == 4 && i < nk && n < p.N) ? sc4[(long long)i * p.lds + n] : __float2half(0.f);
+    };
+    __half s_next = load_scale(0), s_next2 = load_scale(1);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S, a = i % kASlots;
+      const __half s_cur = s_next;
+      s_next = s_next2;
+      s_next2 = load_scale(i + 2);
+      mbar_wait(full + s, (i / S) & 1, p.err, kDevErrFullWait);
+      const uint32_t wrow = smem_u32(smem + (size_t)s * L::kStage + L::kXStage);
+      uint32_t cols[64];
+      if (WBITS == 4) {
+        // 64 bytes of row r, 64-byte swizzle: chunk q at (q ^ ((r >> 1) & 3))
+        uint32_t wd[16];
+        #pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = lds128(wrow + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
+          wd[4 * q] = v.x; wd[4 * q + 1] = v.y; wd[4 * q + 2] = v.z; wd[4 * q + 3] = v.w;
+        }
+        const uint32_t s2 = (uint32_t)__half_as_ushort(s_cur) * 0x00010001u;
+        #pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          if (LAYOUT == 0) {
+            // bytes 4w..4w+3: low nibbles k = 4w.., high nibbles k = 64+4w..
+            uint32_t lo01, lo23, hi01, hi23;
+            dec_w4_split(wd[w], lo01, lo23, hi01, hi23);
+            cols[2 * w] = h2_mul(lo01, s2);
+            cols[2 * w + 1] = h2_mul(lo23, s2);
+            cols[32 + 2 * w] = h2_mul(hi01, s2);
+            cols[33 + 2 * w] = h2_mul(hi23, s2);
+          } else {
+            // k = 8w .. 8w+7
+            uint32_t p01, p23, p45, p67;
+            dec_w4_adjacent(wd[w], p01, p23, p45, p67);
+            cols[4 * w] = h2_mul(p01, s2);
+            cols[4 * w + 1] = h2_mul(p23, s2);
+            cols[4 * w + 2] = h2_mul(p45, s2);
+            cols[4 * w + 3] = h2_mul(p67, s2);
+          }
+        }
+      } else {
+        // 128 bytes of row r, 128-byte swizzle: chunk q at (q ^ (r & 7)); k = 4w..4w+3
+        #pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = lds128(wrow + r * 128 + ((q ^ (r & 7)) << 4));
+          dec_w8(v.x, cols[8 * q + 0], cols[8 * q + 1]);
+          dec_w8(v.y, cols[8 * q + 2], cols[8 * q + 3]);
+          dec_w8(v.z, cols[8 * q + 4], cols[8 * q + 5]);
+          dec_w8(v.w, cols[8 * q + 6], cols[8 * q + 7]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(wfree + s);       // packed tile consumed
+      if (i >= kASlots) mbar_wait(afree + a, ((i / kASlots) - 1) & 1, p.err, kDevErrFullWait);
+      tc_fence_after();
+      const uint32_t a_taddr = tmem + lane_base + L::kACol + 64u * a;
+      #pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint32_t v8[8];
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) v8[e] = cols[8 * c8 + e];
+        tmem_st8(a_taddr + 8u * c8, v8);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(afull + a);
+    }
+
+    // epilogue
+    mbar_wait(dfull, 0, p.err, kDevErrMmaWait);
+    tc_fence_after();
+    float sc8 = 1.f, bv = 0.f;
+    if (n < p.N) {
+      if (WBITS == 8)
+        sc8 = p.scale_f32 ? static_cast<const float*>(p.scale)[n]
+                          : __half2float(static_cast<const __half*>(p.scale)[n]);
+      if (p.bias)
+        bv = p.bias_f32 ? static_cast<const float*>(p.bias)[n]
+                        : __half2float(static_cast<const __half*>(p.bias)[n]);
+    }
+    #pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(tmem + lane_base + (uint32_t)c0, v);
+      tmem_ld_wait();
+      if (n < p.N) {
+        #pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + c0 + j;
+          if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(__uint_as_float(v[j]), sc8, bv));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace gemm
+}  // namespace ql

@@ -64,7 +64,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait on the phase with the given parity.  Returns false (and
-// records `code` in the device error word) when the budget runs out.
+// records `code` in the device error word) when the budget runs out.  Once
+// any wait on the device has given up (error word set), every later slow
+// wait gives up at once, so a broken pipeline ends within one budget.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word,
                                           unsigned code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -73,6 +75,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile unsigned*>(err_word) != 0u) return false;
     if (globaltimer_ns() - t0 > kWaitBudgetNs) {
       atomicCAS(err_word, 0u, code);
       return false;

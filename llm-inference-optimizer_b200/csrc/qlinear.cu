@@ -20,6 +20,7 @@
 #include "../../include/qlinear.h"
 #include "ql_common.cuh"
 #include "qformat.cuh"
+#include "qgemm.cuh"
 #include "qgemv.cuh"
 
 #define QL_VERSION_MAJOR 0
@@ -108,6 +109,37 @@ int make_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uint64_t
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
+}
+
+// Activations [rows][K] fp16 as a 2-D map, box (64 k, box_rows), 128-byte
+// swizzle: the K-major canonical layout the tensor-core B operand reads.
+int make_act_map(CUtensorMap* tm, const void* base, uint64_t K, uint64_t rows, uint64_t ld_elems, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return QL_ERR_DEVICE;
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
+}
+
+// Packed weight rows as [N][kbytes/C][C] with one C-byte stage per row per
+// box (C = 64 for int4, 128 for int8) and the matching swizzle.
+int make_gemm_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uint64_t rows, uint64_t row_stride,
+                         int chunk) {
+  auto fn = encode_fn();
+  if (!fn) return QL_ERR_DEVICE;
+  cuuint64_t dims[3] = {(cuuint64_t)chunk, kbytes / chunk, rows};
+  cuuint64_t strides[2] = {(cuuint64_t)chunk, row_stride};
+  cuuint32_t box[3] = {(cuuint32_t)chunk, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, chunk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
 }
@@ -387,6 +419,76 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
                     : launch_gemv_t<4, 1, 2>(pl, tm, p, a.stream, pdl);
 }
 
+template <int WBITS, int LAYOUT, int BN>
+int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm) {
+  using L = ql::gemm::Layout<WBITS, BN>;
+  auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
+  int S = (int)std::min<size_t>(6, (kSmemOptin - 1024 - 256) / L::kStage);
+  if (S < 2) return QL_ERR_UNSUPPORTED;
+  prm.stages = S;
+  static std::atomic<unsigned char> done[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!done[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) != cudaSuccess) {
+      cudaGetLastError();
+      return QL_ERR_CUDA;
+    }
+    done[dev].store(1, std::memory_order_release);
+  }
+  dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN));
+  if (grid.y > 65535) return QL_ERR_BAD_SHAPE;
+  return launch(kern, grid, dim3(ql::gemm::kThreads), L::smem_bytes(S), a.stream, (a.flags & QL_FLAG_PDL) != 0,
+                tx, tw, prm);
+}
+
+// Tensor-core path eligibility: int4 always (K % 128 == 0); int8 needs
+// K % 128 == 0 so a stage is one 128-byte run of every row.
+bool gemm_ok(const LinearArgs& a) {
+  const int64_t kbytes = a.wbits == 4 ? a.K / 2 : a.K;
+  return a.K % 128 == 0 && kbytes % (a.wbits == 4 ? 64 : 128) == 0 && a.N <= INT_MAX && a.M <= 65535LL * 128;
+}
+
+template <int WBITS, int LAYOUT>
+int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, int bn) {
+  const uint64_t kbytes = WBITS == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
+  CUtensorMap tx, tw;
+  int st = make_act_map(&tx, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx, bn);
+  if (st != QL_OK) return st;
+  st = make_gemm_weight_map(&tw, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, WBITS == 4 ? 64 : 128);
+  if (st != QL_OK) return st;
+  ql::gemm::Params p;
+  p.scale = a.scale;
+  p.bias = a.bias;
+  p.out = static_cast<__half*>(a.out);
+  p.lds = a.lds;
+  p.ldo = a.ldo;
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.nk = (int)(a.K / 128);
+  p.stages = 0;
+  p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
+  p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  p.err = dev->err_word;
+  switch (bn) {
+    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p);
+    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p);
+    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p);
+    default: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p);
+  }
+}
+
+int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
+  const int bn = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+  if (a.wbits == 8) return run_gemm_layout<8, 0>(a, dev, bn);
+  if (a.layout == QL_W4_LAYOUT_SPLIT_HALF) return run_gemm_layout<4, 0>(a, dev, bn);
+  return run_gemm_layout<4, 1>(a, dev, bn);
+}
+
+// Batch size from which the tensor-core GEMM replaces the decode kernel.
+constexpr int64_t kGemmMinM = 65;
+
 int run_linear(const LinearArgs& a) {
   if (!a.x || !a.w || !a.scale || !a.out) {
     if (a.M == 0 || a.N == 0) return QL_OK;
@@ -407,10 +509,14 @@ int run_linear(const LinearArgs& a) {
   int st;
   DeviceInfo* dev = current_device(&st);
   if (!dev) return st;
-  if (a.flags & QL_FLAG_FORCE_GEMM) return QL_ERR_UNSUPPORTED;
   const bool fast_ok = a.K > 0 && aligned16(a.x) && a.ldx % 8 == 0 && a.K % 8 == 0 && aligned16(a.w) &&
                        a.ldw % 16 == 0 && wrow % 16 == 0;
+  if (a.flags & QL_FLAG_FORCE_GEMM) {
+    if (!fast_ok || !gemm_ok(a)) return QL_ERR_UNSUPPORTED;
+    return run_gemm(a, dev);
+  }
   if ((a.flags & QL_FLAG_FORCE_GENERIC) || !fast_ok) return run_generic(a);
+  if (!(a.flags & QL_FLAG_FORCE_GEMV) && a.M >= kGemmMinM && gemm_ok(a)) return run_gemm(a, dev);
   return run_gemv(a, dev);
 }
 
