@@ -412,6 +412,79 @@ def run_ours(args):
     return 0
 
 
+PREFILL_MS = (512, 2048, 8192)
+PREFILL_SHAPES = ((1536, 8960), (8960, 1536), (4096, 14336), (14336, 4096))   # (K, N)
+
+
+def prefill_measure(reps=5, wbits_list=(4, 8), ms=PREFILL_MS, shapes=PREFILL_SHAPES):
+    """dequant-fused GEMM on the tensor cores.  Per
+    (wbits, shape, M): best of `reps` CUDA-event timings of one launch, with
+    L2 flushed (256 MB write) before every timed launch.  Returns
+    {key: {"us": t, "TFLOPS": 2MNK/t}} and the aggregate TFLOPS."""
+    import torch
+    from qlinear.kernels.w4a16_matmul import w4a16_linear, w4a16_quantize_cuda
+    from qlinear.kernels.w8a16_matmul import w8a16_linear, w8a16_quantize_cuda
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(11)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    tot_flop = 0.0
+    tot_s = 0.0
+    for wbits in wbits_list:
+        for K, N in shapes:
+            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+            a, b = w4a16_quantize_cuda(w) if wbits == 4 else w8a16_quantize_cuda(w)
+            del w
+            fn = w4a16_linear if wbits == 4 else w8a16_linear
+            for M in ms:
+                x = torch.randn(M, K, generator=gen, device=dev).half()
+                y = torch.empty(M, N, dtype=torch.float16, device=dev)
+                fn(x, a, b, out=y)
+                best = 1e30
+                for _ in range(reps):
+                    flush.fill_(1)
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn(x, a, b, out=y)
+                    e1.record()
+                    torch.cuda.synchronize(dev)
+                    best = min(best, e0.elapsed_time(e1) * 1e-3)
+                flop = 2.0 * M * N * K
+                out[f"w{wbits}_M{M}_K{K}_N{N}"] = {"us": round(best * 1e6, 2), "TFLOPS": round(flop / best / 1e12, 1)}
+                tot_flop += flop
+                tot_s += best
+                del x, y
+            del a, b
+    del flush
+    return out, tot_flop / tot_s / 1e12
+
+
+def run_prefill(args):
+    """`--workload prefill`: BASELINE config 3 as its own JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    detail, agg = prefill_measure(reps=max(3, args.steps))
+    peak = measured_tflops()
+    print(json.dumps({
+        "metric": METRIC, "value": agg, "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": 1,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config3: W4A16/W8A16 prefill GEMM, M in {512,2048,8192}, (K,N) in "
+                               "{(1536,8960),(8960,1536),(4096,14336),(14336,4096)}, L2 flushed per launch"},
+        "roofline": {"bound": "tensor", "achieved": agg, "peak": peak[0], "unit": "TFLOP/s",
+                     "frac": agg / peak[0], "peak_kind": peak[1]},
+        "detail": detail}), flush=True)
+    return 0
+
+
+def measured_tflops() -> tuple[float, str]:
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def run_profile_one(args):
     """A handful of eager launches of one (wbits, M, K, N) layer with its
     weights cycled over enough copies to exceed L2: the small case that the
@@ -449,11 +522,14 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("config1", "prefill"), default="config1")
     ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
                     help="a few eager launches of one layer shape (small case for ncu)")
     args = ap.parse_args()
     if args.profile_one:
         return run_profile_one(args)
+    if args.workload == "prefill" and args.impl == "ours":
+        return run_prefill(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
