@@ -138,6 +138,36 @@ size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes,
                  int64_t* fields, int nfields);
 
+/* ----------------------------------------------- no-allocation variant */
+/* Size of the fixed scratch array behind ql_w4a16_linear_static_ws. */
+#define QL_STATIC_WS_BYTES (2u * 1024u * 1024u)
+/*
+ * ql_w4a16_linear without a workspace argument: the split-K scratch comes
+ * from one fixed QL_STATIC_WS_BYTES array compiled into the library, so the
+ * call needs no device memory beyond the caller's inputs and outputs.  No
+ * counterpart in the reference (its Triton launcher needs no scratch).
+ * It exists for callers that cannot allocate device memory when they call
+ * in and have no spare buffer to hand over: code embedded in a host
+ * program or framework that owns every device allocation, or a serving
+ * loop where a cudaMalloc/cudaFree (which can synchronise the whole
+ * device) is not acceptable in the request path.
+ *   - It never calls cudaMalloc, cudaFree or any allocating routine.
+ *   - Shapes whose fastest plan needs more scratch than QL_STATIC_WS_BYTES
+ *     return QL_ERR_WORKSPACE and launch nothing.
+ *   - The first call on a device looks up the array's device address and
+ *     clears it on `stream`; make that first call before any stream capture.
+ *   - All calls on a device share the array.  Each call leaves it zeroed for
+ *     the next, but calls that overlap on the GPU (e.g. on two streams) race.
+ */
+int ql_w4a16_linear_static_ws(const void* x, int x_dtype,
+                              const void* w_packed, int layout,
+                              const void* scales,
+                              const void* bias, int bias_dtype,
+                              void* out,
+                              int64_t M, int64_t N, int64_t K,
+                              int64_t ldx, int64_t ldw, int64_t lds, int64_t ldo,
+                              unsigned flags, void* stream);
+
 /* -------------------------------------------------------- format helpers */
 /* out_f32[N, K] = w_q * scale (fp32), bit-exact with the reference. */
 int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype,

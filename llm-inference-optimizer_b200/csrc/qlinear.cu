@@ -30,6 +30,10 @@
 // Device-global error word written by bounded waits that run out.
 __device__ unsigned g_ql_device_error;
 
+// Fixed split-K scratch of ql_w4a16_linear_static_ws: one array per device,
+// shared by every call of that entry point on the device.
+static __device__ __align__(256) unsigned char g_ql_static_ws[QL_STATIC_WS_BYTES];
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -653,6 +657,50 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int qmin
   return launch(ql::fmt::quantize_int4_kernel, dim3((unsigned)cdiv(G, 4), (unsigned)N), dim3(128), 0,
                 static_cast<cudaStream_t>(stream), false, static_cast<const __half*>(w), (long long)ldw, (int)K,
                 qmin, layout, w_packed, static_cast<__half*>(scales), (int)N);
+}
+
+// Once per device, with that device current: the host-side name of
+// g_ql_static_ws is only a stand-in, so its device address is looked up
+// here, checked, and the array is cleared on the first caller's stream.
+struct StaticWs {
+  std::once_flag once;
+  int status = QL_OK;
+  void* ptr = nullptr;
+};
+static StaticWs g_static_ws[kMaxDevices];
+
+int ql_w4a16_linear_static_ws(const void* x, int x_dtype, const void* w_packed, int layout, const void* scales,
+                              const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K,
+                              int64_t ldx, int64_t ldw, int64_t lds, int64_t ldo, unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  if (workspace_size(4, M, N, K) > QL_STATIC_WS_BYTES) return QL_ERR_WORKSPACE;
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  StaticWs& w = g_static_ws[d];
+  std::call_once(w.once, [&] {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_ql_static_ws) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      w.status = QL_ERR_CUDA;
+      return;
+    }
+    if (cudaMemsetAsync(ptr, 0, QL_STATIC_WS_BYTES, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+      cudaGetLastError();
+      w.status = QL_ERR_CUDA;
+      return;
+    }
+    w.ptr = ptr;
+  });
+  if (w.status != QL_OK) return w.status;
+  LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, out, M, N, K, ldx, ldw, lds,
+               ldo, w.ptr, (size_t)QL_STATIC_WS_BYTES, flags, static_cast<cudaStream_t>(stream)};
+  return run_linear(a);
 }
 
 const char* ql_strerror(int status) {

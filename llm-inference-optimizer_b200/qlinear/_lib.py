@@ -30,6 +30,8 @@ QL_DTYPE_F16 = 0
 QL_DTYPE_F32 = 1
 QL_DTYPE_BF16 = 2
 
+QL_STATIC_WS_BYTES = 2 * 1024 * 1024
+
 QL_W4_LAYOUT_SPLIT_HALF = 0
 QL_W4_LAYOUT_ADJACENT = 1
 
@@ -50,6 +52,8 @@ SIGNATURES = {
                                _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
     "ql_w4a16_linear": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp,
                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
+    "ql_w4a16_linear_static_ws": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _uint, _vp]),
     "ql_w8a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_w4a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_gemv_plan": (_int, [_int, _i64, _i64, _i64, _sz, ctypes.POINTER(_i64), _int]),
