@@ -12,16 +12,18 @@
 //     packed weight tile (128 rows x 64 B int4 / 128 B int8, 64/128-byte
 //     swizzle, a 3-D view of the rows) and the activation tile (BN rows x
 //     128 k as two 128-byte-swizzled K-major atoms).
-//   * warps 2-5 (128 threads, thread = weight row = TMEM lane): read their
-//     row's packed bytes, decode them to fp16 in registers (int4: times
-//     the fp16 group scale, one rounding per weight; int8: exact) and write
-//     them into TMEM with tcgen05.st — the A operand never touches shared
-//     memory, which keeps shared-memory bandwidth for the activations.
+//   * warps 2-9 (256 threads; thread = weight row = TMEM lane, two warps per
+//     lane quarter, each decoding one half of the stage's 128 k): read the
+//     row's packed bytes, decode them to fp16 in registers (int4: times the
+//     fp16 group scale, one rounding per weight; int8: exact) and write them
+//     into TMEM with tcgen05.st — the A operand never touches shared memory,
+//     which keeps shared-memory bandwidth for the activations.
 //   * warp 1 (one thread): issues tcgen05.mma.cta_group::1.kind::f16
 //     (A from TMEM, B from shared memory by descriptor, fp32 accumulator
 //     in TMEM) and tcgen05.commit's the stage back to producer/dequant.
-//   * epilogue (warps 2-5): tcgen05.ld of the accumulator, int8 row scale
-//     and bias in fp32, fp16 store (32 consecutive n per warp per row).
+//   * epilogue (warps 2-9, each half of the activation columns): tcgen05.ld
+//     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
+//     consecutive n per warp per activation row).
 // No cluster multicast anywhere; every wait is bounded.
 #pragma once
 
@@ -32,7 +34,7 @@ namespace gemm {
 
 constexpr int kTileN = 128;     // weight rows per CTA = UMMA M
 constexpr int kBK = 128;        // k per stage = 8 MMAs of K=16
-constexpr int kThreads = 192;   // 6 warps
+constexpr int kThreads = 320;   // 10 warps: producer, MMA, 8 dequant/epilogue
 constexpr int kASlots = 2;      // A (dequantized weight) stages in TMEM
 
 struct Params {
@@ -142,11 +144,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(wfree + s, 4);
+      mbar_init(wfree + s, 8);
       mbar_init(xfree + s, 1);
     }
     for (int a = 0; a < kASlots; ++a) {
-      mbar_init(afull + a, 4);
+      mbar_init(afull + a, 8);
       mbar_init(afree + a, 1);
     }
     mbar_init(dfull, 1);
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------ dequant + epilogue
     const int quarter = warp & 3;                 // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;             // which 64 k of the stage (and half of the columns)
     const int r = quarter * 32 + lane;            // weight row within the tile = TMEM lane
     const int n = n0 + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -222,54 +225,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_next2 = load_scale(i + 2);
       mbar_wait(full + s, (i / S) & 1, p.err, kDevErrFullWait);
       const uint32_t wrow = smem_u32(smem + (size_t)s * L::kStage + L::kXStage);
-      uint32_t cols[64];
+      uint32_t cols[32];                          // columns 32*half .. +32 of the A stage: k = 64*half ..
       if (WBITS == 4) {
-        // 64 bytes of row r, 64-byte swizzle: chunk q at (q ^ ((r >> 1) & 3))
-        uint32_t wd[16];
-        #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 v = lds128(wrow + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
-          wd[4 * q] = v.x; wd[4 * q + 1] = v.y; wd[4 * q + 2] = v.z; wd[4 * q + 3] = v.w;
-        }
         const uint32_t s2 = (uint32_t)__half_as_ushort(s_cur) * 0x00010001u;
-        #pragma unroll
-        for (int w = 0; w < 16; ++w) {
-          if (LAYOUT == 0) {
-            // bytes 4w..4w+3: low nibbles k = 4w.., high nibbles k = 64+4w..
-            uint32_t lo01, lo23, hi01, hi23;
-            dec_w4_split(wd[w], lo01, lo23, hi01, hi23);
-            cols[2 * w] = h2_mul(lo01, s2);
-            cols[2 * w + 1] = h2_mul(lo23, s2);
-            cols[32 + 2 * w] = h2_mul(hi01, s2);
-            cols[33 + 2 * w] = h2_mul(hi23, s2);
-          } else {
-            // k = 8w .. 8w+7
-            uint32_t p01, p23, p45, p67;
-            dec_w4_adjacent(wd[w], p01, p23, p45, p67);
-            cols[4 * w] = h2_mul(p01, s2);
-            cols[4 * w + 1] = h2_mul(p23, s2);
-            cols[4 * w + 2] = h2_mul(p45, s2);
-            cols[4 * w + 3] = h2_mul(p67, s2);
+        if (LAYOUT == 0) {
+          // all 64 bytes of row r (64-byte swizzle: chunk q at q ^ ((r >> 1) & 3)); half 0 takes the
+          // low nibbles (k = 4w..4w+3), half 1 the high nibbles (k = 64+4w..)
+          #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v = lds128(wrow + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int w = 4 * q + e;
+              const uint32_t t0 = __byte_perm(wd[e], 0u, 0x1100), t1 = __byte_perm(wd[e], 0u, 0x3322);
+              if (half == 0) {
+                cols[2 * w] = h2_mul(h2_sub(lop3_and_or(t0, 0x000F000Fu, kH2Magic), kH2_1032), s2);
+                cols[2 * w + 1] = h2_mul(h2_sub(lop3_and_or(t1, 0x000F000Fu, kH2Magic), kH2_1032), s2);
+              } else {
+                cols[2 * w] = h2_mul(h2_fma(lop3_and_or(t0, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
+                cols[2 * w + 1] = h2_mul(h2_fma(lop3_and_or(t1, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
+              }
+            }
+          }
+        } else {
+          // bytes 32*half .. +32 of row r: k = 64*half + 8w' .. +7
+          #pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int q = 2 * half + q2;
+            const uint4 v = lds128(wrow + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int w = 4 * q2 + e;
+              uint32_t p01, p23, p45, p67;
+              dec_w4_adjacent(wd[e], p01, p23, p45, p67);
+              cols[4 * w] = h2_mul(p01, s2);
+              cols[4 * w + 1] = h2_mul(p23, s2);
+              cols[4 * w + 2] = h2_mul(p45, s2);
+              cols[4 * w + 3] = h2_mul(p67, s2);
+            }
           }
         }
       } else {
-        // 128 bytes of row r, 128-byte swizzle: chunk q at (q ^ (r & 7)); k = 4w..4w+3
+        // bytes 64*half .. +64 of row r (128-byte swizzle: chunk q at q ^ (r & 7)); k = 64*half + 4w'..
         #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const int q = 4 * half + q2;
           const uint4 v = lds128(wrow + r * 128 + ((q ^ (r & 7)) << 4));
-          dec_w8(v.x, cols[8 * q + 0], cols[8 * q + 1]);
-          dec_w8(v.y, cols[8 * q + 2], cols[8 * q + 3]);
-          dec_w8(v.z, cols[8 * q + 4], cols[8 * q + 5]);
-          dec_w8(v.w, cols[8 * q + 6], cols[8 * q + 7]);
+          dec_w8(v.x, cols[8 * q2 + 0], cols[8 * q2 + 1]);
+          dec_w8(v.y, cols[8 * q2 + 2], cols[8 * q2 + 3]);
+          dec_w8(v.z, cols[8 * q2 + 4], cols[8 * q2 + 5]);
+          dec_w8(v.w, cols[8 * q2 + 6], cols[8 * q2 + 7]);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(wfree + s);       // packed tile consumed
       if (i >= kASlots) mbar_wait(afree + a, ((i / kASlots) - 1) & 1, p.err, kDevErrFullWait);
       tc_fence_after();
-      const uint32_t a_taddr = tmem + lane_base + L::kACol + 64u * a;
+      const uint32_t a_taddr = tmem + lane_base + L::kACol + 64u * a + 32u * half;
       #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         uint32_t v8[8];
         #pragma unroll
         for (int e = 0; e < 8; ++e) v8[e] = cols[8 * c8 + e];
@@ -281,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(afull + a);
     }
 
-    // epilogue
+    // epilogue: this warp stores activation columns [half*BN/2, (half+1)*BN/2)
     mbar_wait(dfull, 0, p.err, kDevErrMmaWait);
     tc_fence_after();
     float sc8 = 1.f, bv = 0.f;
@@ -293,14 +309,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         bv = p.bias_f32 ? static_cast<const float*>(p.bias)[n]
                         : __half2float(static_cast<const __half*>(p.bias)[n]);
     }
+    constexpr int kHalfCols = BN / 2;
     #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(tmem + lane_base + (uint32_t)c0, v);
+    for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+      uint32_t v[8];
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                   : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                     "=r"(v[7])
+                   : "r"(tmem + lane_base + (uint32_t)c0)
+                   : "memory");
       tmem_ld_wait();
       if (n < p.N) {
         #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const int m = m0 + c0 + j;
           if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(__uint_as_float(v[j]), sc8, bv));
         }

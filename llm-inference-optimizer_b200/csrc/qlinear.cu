@@ -428,6 +428,7 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
   using L = ql::gemm::Layout<WBITS, BN>;
   auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
   int S = (int)std::min<size_t>(6, (kSmemOptin - 1024 - 256) / L::kStage);
+  if (S < 3 && BN > 128) return QL_ERR_UNSUPPORTED;
   if (S < 2) return QL_ERR_UNSUPPORTED;
   prm.stages = S;
   static std::atomic<unsigned char> done[kMaxDevices];
@@ -479,12 +480,15 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, int bn) {
     case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p);
     case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p);
     case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p);
-    default: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p);
+    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p);
+    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 128>(a, tx, tw, p);
   }
 }
 
 int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
-  const int bn = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+  // activation rows per CTA; int4 tiles at 256 when the batch fills them
+  // (three 72 KB stages fit), int8 stays at 128 (four 80 KB stages would not)
+  const int bn = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : (a.M <= 128 || a.wbits == 8) ? 128 : 256;
   if (a.wbits == 8) return run_gemm_layout<8, 0>(a, dev, bn);
   if (a.layout == QL_W4_LAYOUT_SPLIT_HALF) return run_gemm_layout<4, 0>(a, dev, bn);
   return run_gemm_layout<4, 1>(a, dev, bn);
