@@ -485,6 +485,121 @@ def measured_tflops() -> tuple[float, str]:
         return 1590.0, "fallback"
 
 
+SHARDED_LAYERS = (("lm_head_1p5b", 1536, 151936, 1), ("lm_head_7b", 4096, 128256, 1),
+                  ("gate_up_7b", 4096, 28672, 2))       # (name, K, N, column groups)
+SHARDED_MS = (1, 16, 64)
+
+
+def layer_bytes(wbits, K, N):
+    """Algorithmic weight bytes of a full layer (all ranks together)."""
+    return N * K // 2 + 2 * N * (K // 128) if wbits == 4 else N * K + 4 * N
+
+
+def run_sharded(args):
+    """`--workload sharded`: BASELINE config 4.  Every rank holds its column
+    shard of each layer (quantized on the device), runs the local kernel and
+    one NCCL all-gather of the fp16 outputs.  Per (wbits, layer, M), three
+    CUDA graphs are timed: local compute only, the all-gather only, and the
+    whole sharded forward; L2 is flushed before every timed replay and the
+    reported time is the max over ranks of each rank's median.  value =
+    total weight bytes of all layers / total end-to-end time (strong
+    scaling: the same layers at every GPU count)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from qlinear.kernels.w4a16_matmul import w4a16_quantize_cuda
+    from qlinear.kernels.w8a16_matmul import w8a16_quantize_cuda
+    from qlinear.quantization.int4 import QuantizedLinearInt4
+    from qlinear.quantization.int8 import QuantizedLinearInt8
+    from qlinear.sharded import ShardedQuantizedLinear, shard_bounds
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(5, args.steps)
+    stream = torch.cuda.Stream(device=dev)
+    detail, graphs = {}, []
+    tot_bytes = 0.0
+    tot_s = 0.0
+
+    def timed(graph):
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1)
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                graph.replay()
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ts.append(e0.elapsed_time(e1) * 1e-3)
+        t = statistics.median(ts)
+        if world > 1:
+            tt = torch.tensor([t], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    for wbits in (4, 8):
+        for name, K, N, groups in SHARDED_LAYERS:
+            n_g = N // groups
+            lo, hi = shard_bounds(n_g, rank, world)
+            rows = groups * (hi - lo)
+            w = (torch.randn(rows, K, generator=gen, device=dev) * 0.02).half()
+            if wbits == 4:
+                mod = QuantizedLinearInt4(*w4a16_quantize_cuda(w), None)
+            else:
+                mod = QuantizedLinearInt8(*w8a16_quantize_cuda(w), None)
+            del w
+            sh = ShardedQuantizedLinear(mod, N, rank, world, groups=groups)
+            for M in SHARDED_MS:
+                x = torch.randn(M, K, generator=gen, device=dev).half()
+                with torch.cuda.stream(stream):
+                    y_loc = sh.local_forward(x)
+                    sh.gather(y_loc)
+                    torch.cuda.synchronize(dev)
+                    g_loc, g_col, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g_loc, stream=stream):
+                        sh.local_forward(x)
+                    with torch.cuda.graph(g_col, stream=stream):
+                        sh.gather(y_loc)
+                    with torch.cuda.graph(g_e2e, stream=stream):
+                        sh(x)
+                graphs += [g_loc, g_col, g_e2e]
+                t_loc, t_col, t_e2e = timed(g_loc), timed(g_col), timed(g_e2e)
+                lb = layer_bytes(wbits, K, N)
+                detail[f"w{wbits}_{name}_M{M}"] = {
+                    "compute_us": round(t_loc * 1e6, 2), "allgather_us": round(t_col * 1e6, 2),
+                    "e2e_us": round(t_e2e * 1e6, 2), "GBps_e2e": round(lb / t_e2e / 1e9, 1),
+                    "GBps_compute_per_gpu": round(lb / world / t_loc / 1e9, 1)}
+                tot_bytes += lb
+                tot_s += t_e2e
+            del sh, mod
+    del graphs
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": reps, "warmup": 1, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config4: column-sharded lm_head 1536->151936, lm_head 4096->128256, fused "
+                                   "gate+up 4096->28672 (2 groups), W4A16 and W8A16, M in {1,16,64}, NCCL "
+                                   "all-gather of fp16 outputs, L2 flushed per replay",
+                       "parallelism": f"column shards x{world}"},
+            "detail": detail}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_profile_one(args):
     """A handful of eager launches of one (wbits, M, K, N) layer with its
     weights cycled over enough copies to exceed L2: the small case that the
@@ -522,7 +637,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("config1", "prefill"), default="config1")
+    ap.add_argument("--workload", choices=("config1", "prefill", "sharded"), default="config1")
     ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
                     help="a few eager launches of one layer shape (small case for ncu)")
     args = ap.parse_args()
@@ -530,6 +645,8 @@ def main():
         return run_profile_one(args)
     if args.workload == "prefill" and args.impl == "ours":
         return run_prefill(args)
+    if args.workload == "sharded" and args.impl == "ours":
+        return run_sharded(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -1,0 +1,92 @@
+"""Column-sharded layers over NCCL on 2 GPUs (skipped with fewer GPUs).
+
+Each rank runs the B200 kernels on its shard; the all-gathered output must
+match the CPU oracle of the full layer, eagerly and replayed from a CUDA
+graph that contains the kernel and the NCCL collective.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import qlinear_oracle as orc
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, result_q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        from qlinear.quantization.int4 import QuantizedLinearInt4
+        from qlinear.quantization.int8 import QuantizedLinearInt8
+        from qlinear.sharded import ShardedQuantizedLinear
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        K, N, M, wbits, groups = case
+        g = torch.Generator().manual_seed(5)
+        lin = torch.nn.Linear(K, N, bias=False).half()
+        with torch.no_grad():
+            lin.weight.copy_((torch.randn(N, K, generator=g) * 0.02).half())
+        q = QuantizedLinearInt4.from_linear(lin) if wbits == 4 else QuantizedLinearInt8.from_linear(lin)
+        x = torch.randn(M, K, generator=g).half()
+        sh = ShardedQuantizedLinear.from_quantized(q, rank, world, groups=groups).cuda()
+        xd = x.cuda()
+        y = sh(xd)
+        # graph replay of the sharded forward (kernel + NCCL all-gather)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            sh(xd)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                yg = sh(xd)
+        torch.cuda.current_stream().wait_stream(s)
+        graph.replay()
+        torch.cuda.synchronize()
+        if wbits == 4:
+            deq = orc.dequantize_int4(q.weight_packed.numpy(), q.scales.numpy())
+        else:
+            deq = orc.dequantize_int8(q.weight_q.numpy(), q.scale.numpy())
+        ref = orc.linear_f32(x.numpy(), deq)
+        ok, max_abs, rel, b_abs, b_rel = orc.check_parity(y.float().cpu().numpy(), ref, x.numpy(), deq)
+        same = torch.equal(y, yg)
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+        result_q.put((rank, bool(ok and same), max_abs, rel))
+    except Exception as e:
+        result_q.put((rank, False, repr(e)[:300], None))
+
+
+@pytest.mark.parametrize("case", [(1536, 8192 + 37, 1, 4, 1), (4096, 2 * 1792, 16, 8, 2), (1536, 4096, 64, 4, 1)])
+def test_sharded_nccl_two_gpus(case):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    res = sorted(q.get() for _ in range(q.qsize()) if True) if not q.empty() else []
+    assert len(res) == 2, (res, [p.exitcode for p in procs])
+    for rank, ok, a, b in res:
+        assert ok, (rank, a, b)
