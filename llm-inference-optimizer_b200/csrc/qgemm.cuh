@@ -24,7 +24,7 @@
 //   * epilogue (warps 2-9, each half of the activation columns): tcgen05.ld
 //     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
-// No cluster multicast anywhere; every wait is bounded.
+// Per-CTA TMA loads only; every wait is bounded.
 #pragma once
 
 #include "ql_common.cuh"

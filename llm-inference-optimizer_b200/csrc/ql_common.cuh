@@ -98,7 +98,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 // 2-D tiled bulk-tensor load global -> shared, completion on an mbarrier.
-// No cluster multicast anywhere in this library.
+// Plain per-CTA loads only (nothing shared across a cluster).
 __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap* tm, int x, int y,
                                             uint64_t* bar, uint64_t policy) {
   asm volatile(
