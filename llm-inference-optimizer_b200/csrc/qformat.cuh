@@ -200,46 +200,47 @@ __global__ void __launch_bounds__(128) quantize_int4_kernel(const __half* w, lon
                                                              int N) {
   const int G = K / 128;
   const int gi = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int n = blockIdx.y;
   const int lane = threadIdx.x & 31;
   if (gi >= G) return;
-  const __half* src = w + (long long)n * ldw + gi * 128 + lane * 4;
-  float v[4];
-  float amax = 0.f;
-  #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = __half2float(src[i]);
-    amax = fmaxf(amax, fabsf(v[i]));
-  }
-  #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const __half s16 = __float2half_rn(fmaxf(__fdiv_rn(amax, 7.0f), 1e-5f));
-  const float s = __half2float(s16);
-  uint32_t q[4];
-  #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float r = rintf(__fdiv_rn(v[i], s));
-    r = fminf(fmaxf(r, (float)qmin), 7.f);
-    q[i] = static_cast<uint32_t>(static_cast<int>(r) + 8);
-  }
-  uint8_t* prow = packed + (long long)n * (K / 2) + gi * 64;
-  if (layout == 0) {
-    // byte j = q[j] | q[j+64] << 4: lanes 0..15 hold k 0..63, lanes 16..31 hold k 64..127
-    uint32_t hi[4];
+  for (int n = blockIdx.y; n < N; n += gridDim.y) {   // rows: grid-stride (gridDim.y <= 65535)
+    const __half* src = w + (long long)n * ldw + gi * 128 + lane * 4;
+    float v[4];
+    float amax = 0.f;
     #pragma unroll
-    for (int i = 0; i < 4; ++i) hi[i] = __shfl_down_sync(0xffffffffu, q[i], 16);
-    if (lane < 16) {
-      uint32_t word = 0;
-      #pragma unroll
-      for (int i = 0; i < 4; ++i) word |= (q[i] | (hi[i] << 4)) << (8 * i);
-      *reinterpret_cast<uint32_t*>(prow + lane * 4) = word;
+    for (int i = 0; i < 4; ++i) {
+      v[i] = __half2float(src[i]);
+      amax = fmaxf(amax, fabsf(v[i]));
     }
-  } else {
-    const uint32_t b0 = q[0] | (q[1] << 4), b1 = q[2] | (q[3] << 4);
-    prow[lane * 2] = static_cast<uint8_t>(b0);
-    prow[lane * 2 + 1] = static_cast<uint8_t>(b1);
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const __half s16 = __float2half_rn(fmaxf(__fdiv_rn(amax, 7.0f), 1e-5f));
+    const float s = __half2float(s16);
+    uint32_t q[4];
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float r = rintf(__fdiv_rn(v[i], s));
+      r = fminf(fmaxf(r, (float)qmin), 7.f);
+      q[i] = static_cast<uint32_t>(static_cast<int>(r) + 8);
+    }
+    uint8_t* prow = packed + (long long)n * (K / 2) + gi * 64;
+    if (layout == 0) {
+      // byte j = q[j] | q[j+64] << 4: lanes 0..15 hold k 0..63, lanes 16..31 hold k 64..127
+      uint32_t hi[4];
+      #pragma unroll
+      for (int i = 0; i < 4; ++i) hi[i] = __shfl_down_sync(0xffffffffu, q[i], 16);
+      if (lane < 16) {
+        uint32_t word = 0;
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) word |= (q[i] | (hi[i] << 4)) << (8 * i);
+        *reinterpret_cast<uint32_t*>(prow + lane * 4) = word;
+      }
+    } else {
+      const uint32_t b0 = q[0] | (q[1] << 4), b1 = q[2] | (q[3] << 4);
+      prow[lane * 2] = static_cast<uint8_t>(b0);
+      prow[lane * 2 + 1] = static_cast<uint8_t>(b1);
+    }
+    if (lane == 0) scales[(long long)gi * N + n] = s16;
   }
-  if (lane == 0) scales[(long long)gi * N + n] = s16;
 }
 
 }  // namespace fmt

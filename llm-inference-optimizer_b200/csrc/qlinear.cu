@@ -650,7 +650,7 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int qmin
                       void* scales, void* stream) {
   if (N == 0 || K == 0) return QL_OK;
   if (!w || !w_packed || !scales) return QL_ERR_NULL_POINTER;
-  if (N < 0 || K < 0 || K % 128 != 0 || N > 65535 || K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (N < 0 || K < 0 || K % 128 != 0 || N > INT_MAX || K > INT_MAX) return QL_ERR_BAD_SHAPE;
   if (ldw < K) return QL_ERR_BAD_STRIDE;
   if (qmin < -8 || qmin > 0) return QL_ERR_UNSUPPORTED;
   if (layout != QL_W4_LAYOUT_SPLIT_HALF && layout != QL_W4_LAYOUT_ADJACENT) return QL_ERR_UNSUPPORTED;
@@ -658,7 +658,8 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int qmin
   int st;
   if (!current_device(&st)) return st;
   const int G = (int)(K / 128);
-  return launch(ql::fmt::quantize_int4_kernel, dim3((unsigned)cdiv(G, 4), (unsigned)N), dim3(128), 0,
+  return launch(ql::fmt::quantize_int4_kernel, dim3((unsigned)cdiv(G, 4), (unsigned)std::min<int64_t>(N, 65535)),
+                dim3(128), 0,
                 static_cast<cudaStream_t>(stream), false, static_cast<const __half*>(w), (long long)ldw, (int)K,
                 qmin, layout, w_packed, static_cast<__half*>(scales), (int)N);
 }

@@ -45,7 +45,7 @@ class QuantizedLinearInt4(nn.Module):
         wt = linear.weight.detach()
         N, K = wt.shape
         assert K % GROUP_SIZE == 0, f"in_features {K} must be a multiple of {GROUP_SIZE}"
-        if wt.is_cuda and wt.dtype == torch.float16 and N > 0 and N <= 65535:
+        if wt.is_cuda and wt.dtype == torch.float16 and N > 0:
             packed, scales = w4a16_quantize_cuda(wt, qmin=qmin, layout=layout)
         else:
             w = wt.float()                                              # (N, K)

@@ -249,3 +249,13 @@ def test_device_quantizer_bitexact():
 
 def test_no_device_error_recorded():
     assert _lib.device_error() == 0
+
+
+def test_device_quantizer_more_rows_than_grid_y():
+    """lm_head-sized row counts (> 65535) go through the grid-stride row loop."""
+    g = torch.Generator().manual_seed(13)
+    w = (torch.randn(70001, 128, generator=g) * 0.02).half()
+    pr, sr = orc.quantize_int4_groups(w.numpy())
+    packed, scales = w4a16_quantize_cuda(w.cuda())
+    assert np.array_equal(packed.cpu().numpy(), pr)
+    assert np.array_equal(scales.cpu().numpy().view(np.uint16), sr.view(np.uint16))
