@@ -364,6 +364,10 @@ def run_ours(args):
                 detail[f"M{M}_K{K}_N{N}"] = {"us_per_launch": round(us, 3), "GBps": round(gbs, 1)}
                 del g
     clocks.stop()
+    from qlinear import _lib
+    dev_err = _lib.device_error()
+    if dev_err != 0:
+        raise RuntimeError(f"device error word {dev_err}: a bounded wait gave up during the bench")
 
     peak, peak_kind = measured_peaks()
     per_rank_gbs = nbytes / (ms_val / args.steps * 1e-3) / 1e9
@@ -524,7 +528,7 @@ def run_sharded(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     reps = max(5, args.steps)
     stream = torch.cuda.Stream(device=dev)
-    detail, graphs = {}, []
+    detail = {}
     tot_bytes = 0.0
     tot_s = 0.0
 
@@ -566,15 +570,23 @@ def run_sharded(args):
                     y_loc = sh.local_forward(x)
                     sh.gather(y_loc)
                     torch.cuda.synchronize(dev)
-                    g_loc, g_col, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                    g_loc, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                    g_col = torch.cuda.CUDAGraph() if world > 1 else None   # no exchange on one GPU
                     with torch.cuda.graph(g_loc, stream=stream):
                         sh.local_forward(x)
-                    with torch.cuda.graph(g_col, stream=stream):
-                        sh.gather(y_loc)
+                    if g_col is not None:
+                        with torch.cuda.graph(g_col, stream=stream):
+                            sh.gather(y_loc)
                     with torch.cuda.graph(g_e2e, stream=stream):
                         sh(x)
-                graphs += [g_loc, g_col, g_e2e]
-                t_loc, t_col, t_e2e = timed(g_loc), timed(g_col), timed(g_e2e)
+                t_loc, t_e2e = timed(g_loc), timed(g_e2e)
+                t_col = timed(g_col) if g_col is not None else 0.0
+                # graphs holding NCCL calls must be gone before the process group is destroyed
+                torch.cuda.synchronize(dev)
+                del g_loc, g_col, g_e2e
+                if rank == 0:
+                    print(f"[sharded] w{wbits} {name} M={M}: local {t_loc * 1e6:.1f} us, all-gather "
+                          f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us", file=sys.stderr, flush=True)
                 lb = layer_bytes(wbits, K, N)
                 detail[f"w{wbits}_{name}_M{M}"] = {
                     "compute_us": round(t_loc * 1e6, 2), "allgather_us": round(t_col * 1e6, 2),
@@ -583,7 +595,10 @@ def run_sharded(args):
                 tot_bytes += lb
                 tot_s += t_e2e
             del sh, mod
-    del graphs
+    from qlinear import _lib
+    dev_err = _lib.device_error()
+    if dev_err != 0:
+        raise RuntimeError(f"device error word {dev_err} after the sharded workload")
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "n_gpus": world,

@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* afree = afull + kASlots;
   uint64_t* dfull = afree + kASlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);   // a wait of this CTA gave up
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(afree + a, 1);
     }
     mbar_init(dfull, 1);
+    *abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
@@ -170,18 +172,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_w = l2_policy_evict_last();   // reused by every activation tile
       const uint64_t pol_x = l2_policy_evict_last();   // reused by every weight tile
       griddep_wait();
+      int issued = 0;
       for (int i = 0; i < nk; ++i) {
         const int s = i % S;
         if (i >= S) {
           const uint32_t par = ((i / S) - 1) & 1;
-          mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait);
-          mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait);
+          if (!mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait, abort) ||
+              !mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort)) {
+            *abort = 1;
+            break;
+          }
         }
         uint8_t* st = smem + (size_t)s * L::kStage;
         mbar_arrive_expect_tx(full + s, L::kTx);
         tma_load_2d(smem_u32(st), &tmap_x, i * kBK, m0, full + s, pol_x);
         tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, i * kBK + 64, m0, full + s, pol_x);
         tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, i, n0, full + s, pol_w);
+        issued = i + 1;
+      }
+      // every issued copy lands before the CTA can exit (only the last
+      // stage of each slot can still be in flight)
+      for (int s = 0; s < min(issued, S); ++s) {
+        const int last = s + ((issued - 1 - s) / S) * S;
+        mbar_wait(full + s, (last / S) & 1, p.err, kDevErrFullWait);
       }
     }
   } else if (warp == 1) {
@@ -190,8 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_f16<BN>();
       for (int i = 0; i < nk; ++i) {
         const int s = i % S, a = i % kASlots;
-        mbar_wait(full + s, (i / S) & 1, p.err, kDevErrMmaWait);
-        mbar_wait(afull + a, (i / kASlots) & 1, p.err, kDevErrMmaWait);
+        if (!mbar_wait(full + s, (i / S) & 1, p.err, kDevErrMmaWait, abort) ||
+            !mbar_wait(afull + a, (i / kASlots) & 1, p.err, kDevErrMmaWait, abort)) {
+          *abort = 1;
+          break;
+        }
         tc_fence_after();
         const uint32_t xs = smem_u32(smem + (size_t)s * L::kStage);
         const uint32_t a_tmem = tmem + L::kACol + 64u * a;
@@ -203,7 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(xfree + s);
         tc_commit(afree + a);
       }
+      // dfull tracks every MMA issued above; waiting for it here means no
+      // MMA is in flight when the TMEM is released, on the error path too
       tc_commit(dfull);
+      mbar_wait(dfull, 0, p.err, kDevErrMmaWait);
     }
   } else {
     // ------------------------------------------------ dequant + epilogue
@@ -223,7 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __half s_cur = s_next;
       s_next = s_next2;
       s_next2 = load_scale(i + 2);
-      mbar_wait(full + s, (i / S) & 1, p.err, kDevErrFullWait);
+      // warp-uniform outcome: tcgen05.st below is warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(full + s, (i / S) & 1, p.err, kDevErrFullWait, abort))) {
+        *abort = 1;
+        break;
+      }
       const uint32_t wrow = smem_u32(smem + (size_t)s * L::kStage + L::kXStage);
       uint32_t cols[32];                          // columns 32*half .. +32 of the A stage: k = 64*half ..
       if (WBITS == 4) {
@@ -281,7 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(wfree + s);       // packed tile consumed
-      if (i >= kASlots) mbar_wait(afree + a, ((i / kASlots) - 1) & 1, p.err, kDevErrFullWait);
+      if (i >= kASlots &&
+          !__all_sync(0xffffffffu, mbar_wait(afree + a, ((i / kASlots) - 1) & 1, p.err, kDevErrFullWait, abort))) {
+        *abort = 1;
+        break;
+      }
       tc_fence_after();
       const uint32_t a_taddr = tmem + lane_base + L::kACol + 64u * a + 32u * half;
       #pragma unroll

@@ -9,7 +9,11 @@
 //     `tpc` consecutive tiles and one K-split of `kb_per_split` k-blocks; a
 //     k-block is 128 bytes of every row (256 k for int4, 128 k for int8).
 //   * Weights stream through shared memory in stages of one tile x
-//     `kb_stage` k-blocks.  Each stage is ONE 3-D TMA box over the rows
+//     `kb_stage` k-blocks.  Every tile has its own P = stages/tpc ring
+//     slots, so each slot is consumed by one tile's warps, in order (a slot
+//     shared by several tiles could be awaited by a faster tile one phase
+//     early, which mbarrier parity cannot tell apart).  Each stage is ONE
+//     3-D TMA box over the rows
 //     viewed as [N][kbytes/C][C] (C = 128, 64, 32 or 16 bytes), so every
 //     request covers 16 runs of kb_stage*128 contiguous bytes — whole rows
 //     when the split spans K — which keeps HBM pages streaming.  Boxes past
@@ -60,7 +64,7 @@ struct Params {
   int tpc;                // tiles per CTA
   int wpt;                // consumer warps per tile
   int kb_stage;           // k-blocks per stage (divides kb_per_split or covers it)
-  int stages;             // ring depth (stages resident at once)
+  int stages;             // ring depth (stages resident at once), a multiple of tpc
   int chunk;              // C: bytes of the innermost tensor-map dimension
   int x_stride;           // halves per staged x row
   int x_rows;             // staged x rows = min(8*MT, M)
@@ -273,6 +277,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.region0 + L.x + L.sc);
   uint64_t* empty = full + stages;
   int* last_flag = reinterpret_cast<int*>(empty + stages);
+  volatile int* abort = last_flag + 1;    // set once a wait of this CTA gives up
 
   const int blk = blockIdx.x, split = blockIdx.y, mchunk = blockIdx.z;
   const int row0 = blk * rows_cta;
@@ -286,12 +291,18 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       mbar_init(full + s, 1);
       mbar_init(empty + s, wpt);
     }
+    *abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
+  // Ring slots per tile: stage (k-chunk kc, tile tt) lives in slot
+  // tt*P + kc%P and is that slot's phase kc/P.
+  const int P = stages / tpc;
+
   // ------------------------------------------------------------ producer
-  // Stage st = kc * tpc + tt holds tile tt, k-blocks [kc*kb_stage, +kb_stage).
+  // Stages are issued in the order st = kc * tpc + tt (tile tt, k-blocks
+  // [kc*kb_stage, +kb_stage)), round-robin over the tiles.
   if (warp == ncw) {
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
@@ -300,13 +311,30 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       if (!p.early_weights) griddep_wait();
       const int per_kb = kBlockBytes / p.chunk;
       const int total = nkc * tpc;
+      int issued = 0;
       for (int st = 0; st < total; ++st) {
-        const int s = st % stages;
-        if (st >= stages) mbar_wait(empty + s, ((st / stages) - 1) & 1, p.err, kDevErrEmptyWait);
         const int kc = st / tpc, tt = st - kc * tpc;
+        const int s = tt * P + kc % P;
+        if (kc >= P && !mbar_wait(empty + s, ((kc / P) - 1) & 1, p.err, kDevErrEmptyWait, abort)) {
+          *abort = 1;
+          break;
+        }
         mbar_arrive_expect_tx(full + s, stage_bytes);
         tma_load_3d(smem_u32(ring + (size_t)s * stage_bytes), &tmap_w, 0, (kb0 + kc * kb_stage) * per_kb,
                     row0 + tt * kTileRows, full + s, pol);
+        issued = st + 1;
+      }
+      // Keep the CTA resident until every issued copy has landed, whatever
+      // the consumers did (in normal operation they have waited for all of
+      // them anyway).  A slot is re-filled only after its previous stage
+      // was consumed, so only the last stage issued on each slot can still
+      // be in flight.
+      for (int tt = 0; tt < tpc && tt < issued; ++tt) {
+        const int kc_last = (issued - 1 - tt) / tpc;          // last k-chunk issued for tile tt
+        for (int j = 0; j < P && j <= kc_last; ++j) {
+          const int kc = kc_last - (kc_last - j) % P;          // last k-chunk issued on slot tt*P+j
+          mbar_wait(full + tt * P + j, (kc / P) & 1, p.err, kDevErrFullWait);
+        }
       }
     }
     return;
@@ -370,10 +398,13 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   const uint32_t rowB_off = (uint32_t)((g + 8) * kb_stage * kBlockBytes);
 
   for (int kc = 0; kc < nkc; ++kc) {
-    const int st = kc * tpc + tt;
-    const int s = st % stages;
-    const bool ok = mbar_wait(full + s, (st / stages) & 1, p.err, kDevErrFullWait);
-    if (ok) {
+    const int s = tt * P + kc % P;
+    // warp-uniform outcome: mma.sync below needs the whole warp
+    if (!__all_sync(0xffffffffu, mbar_wait(full + s, (kc / P) & 1, p.err, kDevErrFullWait, abort))) {
+      *abort = 1;   // stop here without releasing the slot; the producer drains its copies
+      break;
+    }
+    {
       const uint32_t tile_s = ring_s + (uint32_t)s * stage_bytes;
       const int kb_lo = kc * kb_stage;
       const int kb_hi = min(kb_stage, kbc - kb_lo);

@@ -13,7 +13,8 @@ namespace ql {
 
 // ------------------------------------------------------------------ errors
 // Device-global error word.  A kernel whose bounded wait runs out stores a
-// code here (first writer wins) and carries on without trapping.
+// code here (first writer wins), lets its in-flight copies and tensor-core
+// operations finish, and returns without trapping.
 enum DeviceError : unsigned {
   kDevErrNone = 0,
   kDevErrFullWait = 1,      // consumer waited too long for a TMA stage
@@ -22,14 +23,10 @@ enum DeviceError : unsigned {
   kDevErrTmem = 4,          // TMEM allocation failed
 };
 
-// Wall-clock budget of any single bounded wait (nanoseconds, %globaltimer).
-constexpr unsigned long long kWaitBudgetNs = 2000000000ull;   // 2 s
-
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// Budget of any single bounded wait, in SM clock cycles.  %clock64 is
+// per-SM and monotonic: 4e9 cycles is about 2 s at the 1.965 GHz boost
+// clock, and longer when the clock is lower.
+constexpr long long kWaitBudgetCycles = 4000000000ll;
 
 // ------------------------------------------------------------ addressing
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -63,20 +60,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on the phase with the given parity.  Returns false (and
-// records `code` in the device error word) when the budget runs out.  Once
-// any wait on the device has given up (error word set), every later slow
-// wait gives up at once, so a broken pipeline ends within one budget.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word,
-                                          unsigned code) {
+// Bounded wait on the phase with the given parity.  Returns false when the
+// budget runs out (the first code is recorded in the device error word) or,
+// when `abort` is given, as soon as *abort is non-zero (another warp of the
+// same CTA has given up).  The error word is only written here, never read,
+// so an error left behind by an earlier launch cannot end this one's waits.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word, unsigned code,
+                                          const volatile int* abort = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const long long t0 = clock64();
   for (;;) {
     #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile unsigned*>(err_word) != 0u) return false;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+    if (abort != nullptr && *abort != 0) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
       atomicCAS(err_word, 0u, code);
       return false;
     }

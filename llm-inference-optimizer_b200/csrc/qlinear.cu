@@ -267,9 +267,10 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
       p.ws_bytes = gemv_ws_bytes(p);
       if (p.ws_bytes > ws_avail) continue;
-      // stages of one tile x kb_stage k-blocks: the whole slice resident if
-      // it fits next to a second CTA; else the fewest k-chunks that still
-      // double-buffer every tile; else whatever fits at all
+      // stages of one tile x kb_stage k-blocks, P ring slots per tile
+      // (stages = P * tpc): the whole slice resident if it fits next to a
+      // second CTA; else the fewest k-chunks that still double-buffer every
+      // tile; else single-k-block stages with whatever depth fits
       const int chunk = weight_chunk((uint64_t)kbytes);
       if (chunk == 0) continue;
       const ql::gemv::Smem base =
@@ -283,10 +284,10 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
           if (kbs * 128 / chunk > 256) continue;
           const size_t stage_bytes = (size_t)16 * kbs * 128;
           const int fit = (int)std::min<size_t>(64, (budget - fixed) / stage_bytes);
-          const int total = tpc * nkc;
-          if (fit >= total || (nkc > 1 && fit >= 2 * tpc) || (nkc == kbps && fit >= 1)) {
+          const int per_tile = std::min(nkc, fit / tpc);
+          if (per_tile == nkc || (nkc > 1 && per_tile >= 2) || (nkc == kbps && per_tile >= 1)) {
             p.kb_stage = kbs;
-            p.stages = std::min(fit, total);
+            p.stages = per_tile * tpc;
             placed = true;
           }
         }
@@ -373,6 +374,7 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   // no decode plan fits (e.g. a tall K with many batch rows and no
   // workspace for split-K): the portable kernel takes it
   if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return run_generic(a);
+  if (pl.stages < pl.tpc || pl.stages % pl.tpc != 0) return QL_ERR_UNSUPPORTED;   // per-tile ring slots
   CUtensorMap tm;
   const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, pl.chunk, pl.kb_stage);

@@ -259,3 +259,42 @@ def test_device_quantizer_more_rows_than_grid_y():
     packed, scales = w4a16_quantize_cuda(w.cuda())
     assert np.array_equal(packed.cpu().numpy(), pr)
     assert np.array_equal(scales.cpu().numpy().view(np.uint16), sr.view(np.uint16))
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 128256, 16), (1536, 151936, 64), (1536, 151936, 16)])
+def test_multiwave_ring_reuse_repeated(K, N, M):
+    """Multi-wave grids whose per-tile weight rings wrap (single-k-block
+    stages, split-K for K=4096): 40 graph replays give bit-identical
+    outputs, column slices match the oracle, no bounded wait gives up and
+    the split-K workspace is left zeroed."""
+    g = torch.Generator(device="cuda").manual_seed(K + M)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).half()
+    packed, scales = w4a16_quantize_cuda(w)
+    del w
+    plan = _lib.gemv_plan(4, M, N, K)
+    assert plan["stages"] < plan["tiles_per_cta"] * plan["kblocks_per_split"] // plan["kblocks_per_stage"]
+    x = make_x(M, K, seed=K).cuda()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ref = w4a16_linear(x, packed, scales)
+        torch.cuda.synchronize()
+        out = torch.empty_like(ref)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(3):
+                w4a16_linear(x, packed, scales, out=out)
+        for _ in range(40):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref)
+    assert _lib.device_error() == 0
+    xn = x.cpu().numpy()
+    for a, b in ((0, 512), (N - 512, N)):
+        p_np = packed[a:b].cpu().numpy()
+        s_np = scales[:, a:b].cpu().numpy()
+        deq = orc.dequantize_int4(p_np, s_np, 0)
+        assert_parity(ref[:, a:b], orc.linear_f32(xn, deq, None), xn, deq, f"cols {a}:{b}")
+    for buf in _launch._workspaces.values():
+        assert int(buf.count_nonzero()) == 0

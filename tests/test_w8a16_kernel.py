@@ -229,3 +229,39 @@ def test_device_quantizer_and_dequantizer_bitexact():
 
 def test_no_device_error_recorded():
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 128256, 16), (1536, 151936, 64)])
+def test_multiwave_ring_reuse_repeated(K, N, M):
+    """Multi-wave grids whose per-tile weight rings wrap: 40 graph replays
+    give bit-identical outputs, column slices match the oracle, no bounded
+    wait gives up and the split-K workspace is left zeroed."""
+    g = torch.Generator(device="cuda").manual_seed(K + M + 8)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).half()
+    w_q, scale = w8a16_quantize_cuda(w)
+    del w
+    plan = _lib.gemv_plan(8, M, N, K)
+    assert plan["stages"] < plan["tiles_per_cta"] * plan["kblocks_per_split"] // plan["kblocks_per_stage"]
+    x = make_x(M, K, seed=K + 1).cuda()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ref = w8a16_linear(x, w_q, scale)
+        torch.cuda.synchronize()
+        out = torch.empty_like(ref)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(3):
+                w8a16_linear(x, w_q, scale, out=out)
+        for _ in range(40):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref)
+    assert _lib.device_error() == 0
+    xn = x.cpu().numpy()
+    for a, b in ((0, 512), (N - 512, N)):
+        deq = orc.dequantize_int8(w_q[a:b].cpu().numpy(), scale[a:b].cpu().numpy())
+        assert_parity(ref[:, a:b], orc.linear_f32(xn, deq, None), xn, deq, f"cols {a}:{b}")
+    for buf in _launch._workspaces.values():
+        assert int(buf.count_nonzero()) == 0
