@@ -128,10 +128,11 @@ size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
 
 /* The decode-kernel plan the library would use for (wbits, M, N, K) with a
- * workspace of `workspace_bytes` (SIZE_MAX = unlimited), for tuning and
- * tests.  fields[0..11] = tiles of 16 rows per CTA, consumer warps per tile,
- * K-splits, 128-byte k-blocks per split, ring stages, batch tiles of 8 per
- * CTA, batch chunks, CTAs, dynamic shared bytes, workspace bytes, k-blocks
+ * workspace of `workspace_bytes` (SIZE_MAX = unlimited) and 16-byte aligned
+ * int4 scale rows, for tuning and tests.  fields[0..11] = tiles of 16 rows
+ * per block, consumer warps per tile, K-splits, 128-byte k-blocks per split,
+ * ring stages, batch tiles of 8 per CTA, batch chunks, CTAs launched (each
+ * runs one or more blocks), dynamic shared bytes, workspace bytes, k-blocks
  * per stage, bytes of the innermost tensor-map dimension (nfields >= 12).  Has no
  * counterpart in the reference (its Triton configs are fixed in
  * _pick_config, w8a16_matmul_triton.py:89-99). */
@@ -198,7 +199,8 @@ const char* ql_strerror(int status);
 /* Version as (major << 16) | (minor << 8) | patch. */
 int ql_version(void);
 /* Kernels never trap: a bounded wait that runs out records a code in a
- * device-global word and the kernel returns early.  These read (and clear)
+ * device-global word, and the kernel lets its copies in flight land and
+ * returns early.  These read (and clear)
  * that word on the current device; they synchronise the device. */
 int ql_device_error(int* code_out);
 int ql_clear_device_error(void);

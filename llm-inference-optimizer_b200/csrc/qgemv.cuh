@@ -5,36 +5,41 @@
 //  _w4a16_matmul_kernel, src/kernels/w4a16_matmul_triton.py:62-117).
 //
 // Work decomposition
-//   * A "tile" is 16 consecutive weight rows (output columns n).  A CTA owns
-//     `tpc` consecutive tiles and one K-split of `kb_per_split` k-blocks; a
-//     k-block is 128 bytes of every row (256 k for int4, 128 k for int8).
+//   * A "tile" is 16 consecutive weight rows (output columns n); a "block" is
+//     `tpc` consecutive tiles.  The grid is persistent along N: CTA x runs
+//     blocks x, x + gridDim.x, ... of one K-split (gridDim.y) and one batch
+//     chunk (gridDim.z).  A k-block is 128 bytes of every row (256 k for
+//     int4, 128 k for int8); a split covers `kb_per_split` k-blocks.
 //   * Weights stream through shared memory in stages of one tile x
-//     `kb_stage` k-blocks.  Every tile has its own P = stages/tpc ring
-//     slots, so each slot is consumed by one tile's warps, in order (a slot
-//     shared by several tiles could be awaited by a faster tile one phase
-//     early, which mbarrier parity cannot tell apart).  Each stage is ONE
-//     3-D TMA box over the rows
-//     viewed as [N][kbytes/C][C] (C = 128, 64, 32 or 16 bytes), so every
-//     request covers 16 runs of kb_stage*128 contiguous bytes — whole rows
-//     when the split spans K — which keeps HBM pages streaming.  Boxes past
-//     the row end read as zero.  One producer thread issues all stages that
-//     fit up front; with programmatic dependent launch that happens before
-//     the kernel waits for its predecessor (weights do not depend on it).
+//     `kb_stage` k-blocks, each stage ONE 3-D TMA box over the rows viewed as
+//     [N][kbytes/C][C] (C = 128, 64, 32 or 16 bytes; boxes past the row end
+//     or past N read as zero).  For int4 the stage also carries the tile's
+//     fp16 group scales for those k-blocks (a second, 2-D box), so nothing
+//     but TMA touches the weight-side data.  One producer thread issues the
+//     stages of all the CTA's blocks in order, running ahead across block
+//     boundaries as far as the ring allows, and issues before the kernel
+//     waits for its predecessor (programmatic dependent launch): weights
+//     and scales do not depend on it.
+//   * Every tile position has its own P = stages/tpc ring slots, so each
+//     slot is consumed by one tile's warps, in order (a slot shared by
+//     several tiles could be awaited by a faster tile one phase early,
+//     which mbarrier parity cannot tell apart).
 //   * Consumer warps: `wpt` warps per tile split each stage's k-blocks.  A
 //     warp loads 16-byte chunks of rows g and g+8, decodes them in registers
 //     to exact fp16 integers and issues mma.sync m16n8k16 with the weights
-//     as the 16-row A operand and the activations (x slice staged in shared
-//     memory) as the n8 operand ("swap-AB": the batch is the narrow side).
-//     Odd rows load the two 64-byte halves of a k-block in the opposite
-//     order to even rows, so each quarter-warp touches all 32 banks once.
-//     fp32 accumulation; the int4 group scale multiplies each 128-k group
-//     partial in fp32, the int8 row scale multiplies the sum once at the
-//     end — as in the reference kernels.
-//   * Warps of a tile reduce through shared memory in a fixed order.  With
-//     more than one K-split, each CTA writes an fp32 partial to its own
-//     workspace slot and the last CTA to arrive (atomic counter) sums the
-//     slots in slot order, applies scale/bias and zeroes slots and counter,
-//     so the result is deterministic and the workspace stays zeroed.
+//     as the 16-row A operand and the activations (the CTA's x slice,
+//     staged once in shared memory) as the n8 operand ("swap-AB": the batch
+//     is the narrow side).  Odd rows load the two 64-byte halves of a
+//     k-block in the opposite order to even rows, so each quarter-warp
+//     touches all 32 banks once.  fp32 accumulation; the int4 group scale
+//     multiplies each 128-k group partial in fp32, the int8 row scale
+//     multiplies the sum once at the end — as in the reference kernels.
+//   * Per block, the warps of a tile reduce through shared memory in a
+//     fixed order.  With more than one K-split, each CTA writes an fp32
+//     partial to its own workspace slot and the last CTA to arrive (atomic
+//     counter) sums the slots in slot order, applies scale/bias and zeroes
+//     slots and counter, so the result is deterministic and the workspace
+//     stays zeroed.
 #pragma once
 
 #include "ql_common.cuh"
@@ -61,36 +66,46 @@ struct Params {
   int nkb;                // ceil(kbytes / 128)
   int kb_per_split;
   int ks;                 // number of K-splits (gridDim.y)
-  int tpc;                // tiles per CTA
+  int nblk;               // blocks of tpc tiles along N (gridDim.x <= nblk)
+  int tpc;                // tiles per block
   int wpt;                // consumer warps per tile
   int kb_stage;           // k-blocks per stage (divides kb_per_split or covers it)
   int stages;             // ring depth (stages resident at once), a multiple of tpc
   int chunk;              // C: bytes of the innermost tensor-map dimension
   int x_stride;           // halves per staged x row
   int x_rows;             // staged x rows = min(8*MT, M)
+  int scale_tma;          // int4: scales arrive with each stage (else staged per block)
   int scale_f32;          // int8 scale dtype
   int bias_f32;           // bias dtype
   int early_weights;      // stream weights before griddepcontrol.wait
-  uint32_t* counters;     // [gridDim.z * gridDim.x] (ks > 1)
-  float* partials;        // [gridDim.z][gridDim.x][ks][mc][tpc*16] (ks > 1)
+  uint32_t* counters;     // [gridDim.z * nblk] (ks > 1)
+  float* partials;        // [gridDim.z][nblk][ks][mc][tpc*16] (ks > 1)
   unsigned* err;          // device error word
 };
 
+// Bytes of one ring stage: weights, then (int4 with scale_tma) the scale box
+// [2*kb_stage groups][16 rows] fp16, padded to 128 bytes.
+__host__ __device__ inline uint32_t stage_weight_bytes(int kb_stage) {
+  return (uint32_t)(kTileRows * kb_stage * kBlockBytes);
+}
+__host__ __device__ inline uint32_t stage_scale_bytes(int wbits, int scale_tma, int kb_stage) {
+  return (wbits == 4 && scale_tma) ? (uint32_t)((2 * kb_stage * kTileRows * 2 + 127) / 128 * 128) : 0u;
+}
+
 // Shared-memory carve-up, identical on host and device.
 struct Smem {
-  size_t ring, red, region0, x, sc, bars, total;
+  size_t ring, red, x, sc, bars, total;
 };
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 __host__ __device__ inline Smem smem_layout(int wbits, int mc, int x_rows, int tpc, int wpt, int stages,
-                                            int kb_stage, int x_stride, int kb_per_split) {
+                                            int kb_stage, int x_stride, int kb_per_split, int scale_tma) {
   Smem s;
-  s.ring = (size_t)stages * kTileRows * kb_stage * kBlockBytes;
-  s.red = (size_t)tpc * wpt * kTileRows * mc * 4;
-  s.region0 = align_up(s.ring > s.red ? s.ring : s.red, 128);
+  s.ring = (size_t)stages * (stage_weight_bytes(kb_stage) + stage_scale_bytes(wbits, scale_tma, kb_stage));
+  s.red = align_up((size_t)tpc * wpt * kTileRows * mc * 4, 128);
   s.x = align_up((size_t)x_rows * x_stride * 2, 16);
-  s.sc = wbits == 4 ? align_up((size_t)kb_per_split * 2 * tpc * kTileRows * 4, 16) : 0;
+  s.sc = (wbits == 4 && !scale_tma) ? align_up((size_t)kb_per_split * 2 * tpc * kTileRows * 4, 16) : 0;
   s.bars = align_up((size_t)2 * stages * 8 + 16, 16);
-  s.total = 128 /* base alignment slack */ + s.region0 + s.x + s.sc + s.bars;
+  s.total = 128 /* base alignment slack */ + s.ring + s.red + s.x + s.sc + s.bars;
   return s;
 }
 
@@ -139,11 +154,12 @@ __device__ __forceinline__ void u4_to_words(const uint4& v, uint32_t (&w)[4]) {
 // all loaded before any is computed so that their shared-memory loads and
 // mma chains overlap.  Every k-step keeps two independent accumulator
 // chains per batch tile.  `rowA`/`rowB` are the shared addresses of this
-// k-block's 128 bytes in rows g and g+8; `odd` = g & 1.
+// k-block's 128 bytes in rows g and g+8; `odd` = g & 1.  int4: sA[h] / sB[h]
+// are the group scales of rows g / g+8 for the k-block's group h (0, 1).
 template <int WBITS, int LAYOUT, int MT, int NS>
 __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, uint32_t rowB, int i, int h0,
                                        int c, int g, bool odd, uint32_t xs_s, int x_stride, int mvalid,
-                                       const float* scA, const float* scB, int sc_stride) {
+                                       const float (&sA)[2], const float (&sB)[2]) {
   uint32_t wA[NS][4], wB[NS][4];
   if (NS == 2) {
     // even rows read half 0 then 1, odd rows half 1 then 0: a quarter-warp
@@ -208,15 +224,13 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, ui
     }
     #pragma unroll
     for (int n = 0; n < NS; ++n) {
-      const int gl = i * 2 + h0 + n;
-      const float sA = scA[gl * sc_stride];
-      const float sB = scB[gl * sc_stride];
+      const float a_s = sA[h0 + n], b_s = sB[h0 + n];
       #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        acc[n & 1][t][0] = fmaf(part[n][0][t][0] + part[n][1][t][0], sA, acc[n & 1][t][0]);
-        acc[n & 1][t][1] = fmaf(part[n][0][t][1] + part[n][1][t][1], sA, acc[n & 1][t][1]);
-        acc[n & 1][t][2] = fmaf(part[n][0][t][2] + part[n][1][t][2], sB, acc[n & 1][t][2]);
-        acc[n & 1][t][3] = fmaf(part[n][0][t][3] + part[n][1][t][3], sB, acc[n & 1][t][3]);
+        acc[n & 1][t][0] = fmaf(part[n][0][t][0] + part[n][1][t][0], a_s, acc[n & 1][t][0]);
+        acc[n & 1][t][1] = fmaf(part[n][0][t][1] + part[n][1][t][1], a_s, acc[n & 1][t][1]);
+        acc[n & 1][t][2] = fmaf(part[n][0][t][2] + part[n][1][t][2], b_s, acc[n & 1][t][2]);
+        acc[n & 1][t][3] = fmaf(part[n][0][t][3] + part[n][1][t][3], b_s, acc[n & 1][t][3]);
       }
     }
   } else {
@@ -252,10 +266,12 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, ui
   }
 }
 
+
 // MT = number of n8 batch tiles per CTA (mc = 8*MT batch rows per grid.z slice).
 template <int WBITS, int LAYOUT, int MT>
 __global__ void __launch_bounds__(kMaxThreads, 2)
-    qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+    qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
+                 const Params p) {
   constexpr int MC = 8 * MT;
   constexpr int EPK = WBITS == 4 ? 256 : 128;      // k elements per k-block
   constexpr int NS = MT == 1 ? 2 : 1;              // k-steps decoded together
@@ -268,23 +284,33 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_cta = tpc * kTileRows;      // power of two
   const int rows_log2 = 31 - __clz(rows_cta);
-  const uint32_t stage_bytes = static_cast<uint32_t>(kTileRows * kb_stage * kBlockBytes);
+  const bool scale_tma = WBITS == 4 && p.scale_tma != 0;
+  const uint32_t w_bytes = stage_weight_bytes(kb_stage);
+  const uint32_t stage_bytes = w_bytes + stage_scale_bytes(WBITS, p.scale_tma, kb_stage);
+  // bytes the TMA actually delivers per stage (the scale box is not padded)
+  const uint32_t stage_tx = w_bytes + (scale_tma ? (uint32_t)(2 * kb_stage * kTileRows * 2) : 0u);
 
-  const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, kb_stage, p.x_stride, p.kb_per_split);
+  const Smem L = smem_layout(WBITS, MC, p.x_rows, tpc, wpt, stages, kb_stage, p.x_stride, p.kb_per_split,
+                             p.scale_tma);
   uint8_t* ring = smem;
-  __half* xs = reinterpret_cast<__half*>(smem + L.region0);
-  float* ssc = reinterpret_cast<float*>(smem + L.region0 + L.x);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.region0 + L.x + L.sc);
+  float* red = reinterpret_cast<float*>(smem + L.ring);                    // [tpc][wpt][MC][16]
+  __half* xs = reinterpret_cast<__half*>(smem + L.ring + L.red);
+  float* ssc = reinterpret_cast<float*>(smem + L.ring + L.red + L.x);       // per-block scales (fallback)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.ring + L.red + L.x + L.sc);
   uint64_t* empty = full + stages;
   int* last_flag = reinterpret_cast<int*>(empty + stages);
   volatile int* abort = last_flag + 1;    // set once a wait of this CTA gives up
 
-  const int blk = blockIdx.x, split = blockIdx.y, mchunk = blockIdx.z;
-  const int row0 = blk * rows_cta;
+  const int split = blockIdx.y, mchunk = blockIdx.z;
   const int kb0 = split * p.kb_per_split;
   const int kbc = min(p.kb_per_split, p.nkb - kb0);
-  const int nkc = (kbc + kb_stage - 1) / kb_stage;   // k-chunks (stages per tile)
+  const int nkc = (kbc + kb_stage - 1) / kb_stage;   // k-chunks (stages per tile per block)
   const int m0 = mchunk * MC;
+  // Ring slots per tile: the q-th stage of tile position tt (q = it*nkc + kc
+  // for block iteration it, k-chunk kc) lives in slot tt*P + q%P and is that
+  // slot's phase q/P.
+  const int P = stages / tpc;
+  const int nit = (p.nblk - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // blocks of this CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -296,32 +322,32 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   }
   __syncthreads();
 
-  // Ring slots per tile: stage (k-chunk kc, tile tt) lives in slot
-  // tt*P + kc%P and is that slot's phase kc/P.
-  const int P = stages / tpc;
-
   // ------------------------------------------------------------ producer
-  // Stages are issued in the order st = kc * tpc + tt (tile tt, k-blocks
-  // [kc*kb_stage, +kb_stage)), round-robin over the tiles.
+  // Stages are issued in the order (block iteration, k-chunk, tile).
   if (warp == ncw) {
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
+      if (scale_tma) prefetch_tmap(&tmap_s);
       // weights are read once unless several batch chunks share them
       const uint64_t pol = gridDim.z > 1 ? l2_policy_evict_last() : l2_policy_evict_first();
       if (!p.early_weights) griddep_wait();
       const int per_kb = kBlockBytes / p.chunk;
-      const int total = nkc * tpc;
+      const int total = nit * nkc * tpc;
       int issued = 0;
       for (int st = 0; st < total; ++st) {
-        const int kc = st / tpc, tt = st - kc * tpc;
-        const int s = tt * P + kc % P;
-        if (kc >= P && !mbar_wait(empty + s, ((kc / P) - 1) & 1, p.err, kDevErrEmptyWait, abort)) {
+        const int q = st / tpc, tt = st - q * tpc;
+        const int it = q / nkc, kc = q - it * nkc;
+        const int s = tt * P + q % P;
+        if (q >= P && !mbar_wait(empty + s, ((q / P) - 1) & 1, p.err, kDevErrEmptyWait, abort)) {
           *abort = 1;
           break;
         }
-        mbar_arrive_expect_tx(full + s, stage_bytes);
-        tma_load_3d(smem_u32(ring + (size_t)s * stage_bytes), &tmap_w, 0, (kb0 + kc * kb_stage) * per_kb,
-                    row0 + tt * kTileRows, full + s, pol);
+        const int row = ((int)blockIdx.x + it * (int)gridDim.x) * rows_cta + tt * kTileRows;
+        const int kbg = kb0 + kc * kb_stage;               // first k-block of the stage
+        uint8_t* dst = ring + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(full + s, stage_tx);
+        tma_load_3d(smem_u32(dst), &tmap_w, 0, kbg * per_kb, row, full + s, pol);
+        if (scale_tma) tma_load_2d(smem_u32(dst + w_bytes), &tmap_s, row, kbg * 2, full + s, pol);
         issued = st + 1;
       }
       // Keep the CTA resident until every issued copy has landed, whatever
@@ -330,10 +356,10 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       // was consumed, so only the last stage issued on each slot can still
       // be in flight.
       for (int tt = 0; tt < tpc && tt < issued; ++tt) {
-        const int kc_last = (issued - 1 - tt) / tpc;          // last k-chunk issued for tile tt
-        for (int j = 0; j < P && j <= kc_last; ++j) {
-          const int kc = kc_last - (kc_last - j) % P;          // last k-chunk issued on slot tt*P+j
-          mbar_wait(full + tt * P + j, (kc / P) & 1, p.err, kDevErrFullWait);
+        const int q_last = (issued - 1 - tt) / tpc;            // last stage issued for tile tt
+        for (int j = 0; j < P && j <= q_last; ++j) {
+          const int q = q_last - (q_last - j) % P;             // last stage issued on slot tt*P+j
+          mbar_wait(full + tt * P + j, (q / P) & 1, p.err, kDevErrFullWait);
         }
       }
     }
@@ -345,27 +371,30 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   const int tt = warp / wpt, w = warp - tt * wpt;
   const int g = lane >> 2, c = lane & 3;
 
-  // int4 group scales of this CTA's rows and groups -> fp32 in shared
-  // memory.  Scales are static like the weights, so they are loaded before
-  // the dependency wait (under programmatic dependent launch this overlaps
-  // the previous kernel).
-  if (WBITS == 4) {
+  // int4 group scales of one block's rows -> fp32 in shared memory, when
+  // they do not come with the stages (scale rows not 16-byte aligned).
+  auto stage_scales = [&](int blk) {
     const int G = p.K / 128;
     const int g0 = kb0 * 2;
     const int ng = min(kbc * 2, G - g0);
+    const int row0 = blk * rows_cta;
     const __half* sc = static_cast<const __half*>(p.scale);
     for (int idx = ctid; idx < (ng << rows_log2); idx += nct) {
       const int gl = idx >> rows_log2, r = idx & (rows_cta - 1);
       const int n = row0 + r;
       ssc[idx] = n < p.N ? __half2float(sc[(long long)(g0 + gl) * p.lds + n]) : 0.f;
     }
-  }
+  };
+  // scales are static like the weights: the first block's are loaded
+  // before the dependency wait
+  if (WBITS == 4 && !scale_tma) stage_scales(blockIdx.x);
 
   griddep_wait();   // x (and out / workspace) may belong to the previous kernel
 
   const int mvalid = min(MC, p.M - m0);
-  // x slice [m0, m0+mvalid) x [kx0, kx0 + kbc*EPK) -> shared memory; k past
-  // K reads as zero.  Rows >= mvalid are never read.
+  // x slice [m0, m0+mvalid) x [kx0, kx0 + kbc*EPK) -> shared memory, once per
+  // CTA (every block of the CTA uses the same slice); k past K reads as
+  // zero.  Rows >= mvalid are never read.
   {
     const int kx0 = kb0 * EPK;
     const int nvec = kbc * EPK / 8;
@@ -382,30 +411,38 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   named_bar_sync(1, nct);
   griddep_launch_dependents();
 
-  float acc[2][MT][4];
-  #pragma unroll
-  for (int u = 0; u < 2; ++u)
-    #pragma unroll
-    for (int t = 0; t < MT; ++t) acc[u][t][0] = acc[u][t][1] = acc[u][t][2] = acc[u][t][3] = 0.f;
-
   const uint32_t ring_s = smem_u32(ring);
   const uint32_t xs_s = smem_u32(xs);
   const int valid_bytes = p.kbytes - kb0 * kBlockBytes;
   const bool odd = (g & 1) != 0;
-  const float* scA = ssc + tt * kTileRows + g;      // scale of row g of this tile, group 0
-  const float* scB = scA + 8;
   const uint32_t rowA_off = (uint32_t)(g * kb_stage * kBlockBytes);
   const uint32_t rowB_off = (uint32_t)((g + 8) * kb_stage * kBlockBytes);
+  const int nout = mvalid << rows_log2;   // (m, r) pairs of a block, r fastest
 
-  for (int kc = 0; kc < nkc; ++kc) {
-    const int s = tt * P + kc % P;
-    // warp-uniform outcome: mma.sync below needs the whole warp
-    if (!__all_sync(0xffffffffu, mbar_wait(full + s, (kc / P) & 1, p.err, kDevErrFullWait, abort))) {
-      *abort = 1;   // stop here without releasing the slot; the producer drains its copies
-      break;
+  for (int it = 0; it < nit; ++it) {
+    const int blk = (int)blockIdx.x + it * (int)gridDim.x;
+    const int row0 = blk * rows_cta;
+    if (it > 0 && WBITS == 4 && !scale_tma) {
+      stage_scales(blk);
+      named_bar_sync(1, nct);
     }
-    {
+
+    float acc[2][MT][4];
+    #pragma unroll
+    for (int u = 0; u < 2; ++u)
+      #pragma unroll
+      for (int t = 0; t < MT; ++t) acc[u][t][0] = acc[u][t][1] = acc[u][t][2] = acc[u][t][3] = 0.f;
+
+    for (int kc = 0; kc < nkc; ++kc) {
+      const int q = it * nkc + kc;
+      const int s = tt * P + q % P;
+      // warp-uniform outcome: mma.sync below needs the whole warp
+      if (!__all_sync(0xffffffffu, mbar_wait(full + s, (q / P) & 1, p.err, kDevErrFullWait, abort))) {
+        *abort = 1;   // stop here without releasing the slot; the producer drains its copies
+        break;
+      }
       const uint32_t tile_s = ring_s + (uint32_t)s * stage_bytes;
+      const uint32_t sst = tile_s + w_bytes + (uint32_t)g * 2u;   // this lane's row in the scale box
       const int kb_lo = kc * kb_stage;
       const int kb_hi = min(kb_stage, kbc - kb_lo);
       for (int kbl = w; kbl < kb_hi; kbl += wpt) {
@@ -413,90 +450,106 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
         const uint32_t rowA = tile_s + rowA_off + (uint32_t)(kbl * kBlockBytes);
         const uint32_t rowB = tile_s + rowB_off + (uint32_t)(kbl * kBlockBytes);
         const int rem = valid_bytes - i * kBlockBytes;       // > 0
+        float sA[2] = {0.f, 0.f}, sB[2] = {0.f, 0.f};
+        if (WBITS == 4) {
+          if (scale_tma) {
+            // stage scale box: [group within the stage][16 rows] fp16
+            const uint32_t s0 = sst + (uint32_t)(kbl * 2 * kTileRows * 2);
+            sA[0] = lds_f16_as_f32(s0);
+            sB[0] = lds_f16_as_f32(s0 + 16);
+            sA[1] = lds_f16_as_f32(s0 + kTileRows * 2);
+            sB[1] = lds_f16_as_f32(s0 + kTileRows * 2 + 16);
+          } else {
+            const float* scr = ssc + tt * kTileRows + g;
+            sA[0] = scr[(i * 2) * rows_cta];
+            sB[0] = scr[(i * 2) * rows_cta + 8];
+            if (rem > 64) {
+              sA[1] = scr[(i * 2 + 1) * rows_cta];
+              sB[1] = scr[(i * 2 + 1) * rows_cta + 8];
+            }
+          }
+        }
         if (rem > 64) {
           if (NS == 2) {
-            ksteps<WBITS, LAYOUT, MT, 2>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
-                                         rows_cta);
+            ksteps<WBITS, LAYOUT, MT, 2>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, sA, sB);
           } else {
-            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
-                                         rows_cta);
-            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 1, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
-                                         rows_cta);
+            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, sA, sB);
+            ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 1, c, g, odd, xs_s, p.x_stride, mvalid, sA, sB);
           }
         } else {
-          ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, scA, scB,
-                                       rows_cta);
+          ksteps<WBITS, LAYOUT, MT, 1>(acc, rowA, rowB, i, 0, c, g, odd, xs_s, p.x_stride, mvalid, sA, sB);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + s);
-  }
 
-  // ---------------------------------------------- intra-CTA reduction
-  named_bar_sync(1, nct);          // every consumer is done reading the ring
-  float* red = reinterpret_cast<float*>(ring);     // [tpc][wpt][MC][16]
-  {
-    float* mine = red + (size_t)(tt * wpt + w) * MC * kTileRows;
-    #pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const int mm = t * 8 + 2 * c;
-      mine[(mm + 0) * kTileRows + g] = acc[0][t][0] + acc[1][t][0];
-      mine[(mm + 1) * kTileRows + g] = acc[0][t][1] + acc[1][t][1];
-      mine[(mm + 0) * kTileRows + g + 8] = acc[0][t][2] + acc[1][t][2];
-      mine[(mm + 1) * kTileRows + g + 8] = acc[0][t][3] + acc[1][t][3];
-    }
-  }
-  named_bar_sync(1, nct);
-
-  const int nout = mvalid << rows_log2;   // (m, r) pairs of this CTA, r fastest
-  if (p.ks == 1) {
-    for (int idx = ctid; idx < nout; idx += nct) {
-      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
-      const int t = r >> 4, rr = r & 15;
-      float v = 0.f;
-      for (int w2 = 0; w2 < wpt; ++w2) v += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
-      const int n = row0 + r;
-      if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
-    }
-    return;
-  }
-
-  // ----------------------------------------- cross-CTA split-K reduction
-  const int slot_elems = MC << rows_log2;
-  const size_t tile_id = (size_t)mchunk * gridDim.x + blk;
-  float* slots = p.partials + tile_id * p.ks * slot_elems;
-  {
-    float* mine = slots + (size_t)split * slot_elems;
-    for (int idx = ctid; idx < nout; idx += nct) {
-      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
-      const int t = r >> 4, rr = r & 15;
-      float v = 0.f;
-      for (int w2 = 0; w2 < wpt; ++w2) v += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
-      mine[idx] = v;
-    }
-  }
-  __threadfence();
-  named_bar_sync(1, nct);
-  if (ctid == 0) {
-    const unsigned old = atomicAdd(p.counters + tile_id, 1u);
-    *last_flag = (old == (unsigned)(p.ks - 1));
-  }
-  named_bar_sync(1, nct);
-  if (*last_flag) {
-    __threadfence();
-    for (int idx = ctid; idx < nout; idx += nct) {
-      float v = 0.f;
-      for (int s2 = 0; s2 < p.ks; ++s2) {
-        float* slot = slots + (size_t)s2 * slot_elems + idx;
-        v += __ldcg(slot);
-        __stcg(slot, 0.f);                       // leave the workspace zeroed
+    // -------------------------------------------------- block epilogue
+    {
+      float* mine = red + (size_t)(tt * wpt + w) * MC * kTileRows;
+      #pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const int mm = t * 8 + 2 * c;
+        mine[(mm + 0) * kTileRows + g] = acc[0][t][0] + acc[1][t][0];
+        mine[(mm + 1) * kTileRows + g] = acc[0][t][1] + acc[1][t][1];
+        mine[(mm + 0) * kTileRows + g + 8] = acc[0][t][2] + acc[1][t][2];
+        mine[(mm + 1) * kTileRows + g + 8] = acc[0][t][3] + acc[1][t][3];
       }
-      const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
-      const int n = row0 + r;
-      if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
     }
-    if (ctid == 0) p.counters[tile_id] = 0u;     // leave the workspace zeroed
+
+    if (p.ks == 1) {
+      // Only the warps of one tile meet here (named barrier 2 + tt), so
+      // tiles finish their blocks independently.
+      if (wpt > 1) named_bar_sync(2 + tt, wpt * 32); else __syncwarp();
+      for (int idx = w * 32 + lane; idx < mvalid * kTileRows; idx += wpt * 32) {
+        const int m = idx >> 4, rr = idx & 15;
+        float v = 0.f;
+        for (int w2 = 0; w2 < wpt; ++w2) v += red[((tt * wpt + w2) * MC + m) * kTileRows + rr];
+        const int n = row0 + tt * kTileRows + rr;
+        if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+      }
+      if (wpt > 1) named_bar_sync(2 + tt, wpt * 32); else __syncwarp();   // red is reused next block
+      if (WBITS == 4 && !scale_tma) named_bar_sync(1, nct);               // so are the block scales
+    } else {
+      named_bar_sync(1, nct);
+      // ------------------------------------- cross-CTA split-K reduction
+      const int slot_elems = MC << rows_log2;
+      const size_t tile_id = (size_t)mchunk * p.nblk + blk;
+      float* slots = p.partials + tile_id * p.ks * slot_elems;
+      {
+        float* mine = slots + (size_t)split * slot_elems;
+        for (int idx = ctid; idx < nout; idx += nct) {
+          const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
+          const int t = r >> 4, rr = r & 15;
+          float v = 0.f;
+          for (int w2 = 0; w2 < wpt; ++w2) v += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
+          mine[idx] = v;
+        }
+      }
+      __threadfence();
+      named_bar_sync(1, nct);
+      if (ctid == 0) {
+        const unsigned old = atomicAdd(p.counters + tile_id, 1u);
+        *last_flag = (old == (unsigned)(p.ks - 1));
+      }
+      named_bar_sync(1, nct);
+      if (*last_flag) {
+        __threadfence();
+        for (int idx = ctid; idx < nout; idx += nct) {
+          float v = 0.f;
+          for (int s2 = 0; s2 < p.ks; ++s2) {
+            float* slot = slots + (size_t)s2 * slot_elems + idx;
+            v += __ldcg(slot);
+            __stcg(slot, 0.f);                       // leave the workspace zeroed
+          }
+          const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
+          const int n = row0 + r;
+          if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+        }
+        if (ctid == 0) p.counters[tile_id] = 0u;     // leave the workspace zeroed
+      }
+      named_bar_sync(1, nct);   // red, the block scales and last_flag are reused by the next block
+    }
   }
 }
 

@@ -117,6 +117,21 @@ int make_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uint64_t
   return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
 }
 
+// int4 group scales [G][lds] fp16 as a 2-D map (inner dimension n), box
+// (16 rows, 2*kb_stage groups): the scales of one tile for one stage.
+int make_scale_map(CUtensorMap* tm, const void* base, uint64_t N, uint64_t G, uint64_t lds, int kb_stage) {
+  auto fn = encode_fn();
+  if (!fn) return QL_ERR_DEVICE;
+  cuuint64_t dims[2] = {N, G};
+  cuuint64_t strides[1] = {lds * 2};
+  cuuint32_t box[2] = {16, (cuuint32_t)(2 * kb_stage)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_OK : QL_ERR_UNSUPPORTED;
+}
+
 // Activations [rows][K] fp16 as a 2-D map, box (64 k, box_rows), 128-byte
 // swizzle: the K-major canonical layout the tensor-core B operand reads.
 int make_act_map(CUtensorMap* tm, const void* base, uint64_t K, uint64_t rows, uint64_t ld_elems, int box_rows) {
@@ -191,8 +206,8 @@ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // ------------------------------------------------------------- GEMV plan
 struct GemvPlan {
   int tpc = 0, wpt = 0, ks = 0, kbps = 0, stages = 0, kb_stage = 0, chunk = 0, mt = 0, mchunks = 0;
-  int x_stride = 0, x_rows = 0, nblk = 0, nkb = 0;
-  size_t smem = 0, ws_bytes = 0, ws_counters = 0;
+  int x_stride = 0, x_rows = 0, nblk = 0, gx = 0, nkb = 0, scale_tma = 0;
+  size_t smem = 0, ws_bytes = 0;
   double cost = 0;
 };
 
@@ -204,26 +219,32 @@ size_t gemv_ws_bytes(const GemvPlan& p) {
 }
 
 // Optional override for tuning sweeps: QLINEAR_GEMV_PLAN="tpc,ks" (ks = 0
-// lets the planner choose).  Read once.
+// lets the planner choose).  When the variable is set at the first call it
+// is re-read on every call (so a sweep can change it); otherwise never again.
 void plan_override(int* tpc, int* ks) {
-  static int o_tpc = -1, o_ks = -1;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    const char* e = std::getenv("QLINEAR_GEMV_PLAN");
-    if (e && std::sscanf(e, "%d,%d", &o_tpc, &o_ks) != 2) o_tpc = o_ks = -1;
-  });
-  *tpc = o_tpc;
-  *ks = o_ks;
+  static std::atomic<int> mode{-1};   // -1 unknown, 0 unset, 1 tuning
+  int m = mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    m = std::getenv("QLINEAR_GEMV_PLAN") ? 1 : 0;
+    mode.store(m, std::memory_order_relaxed);
+  }
+  *tpc = *ks = -1;
+  if (m == 0) return;
+  const char* e = std::getenv("QLINEAR_GEMV_PLAN");
+  if (e && std::sscanf(e, "%d,%d", tpc, ks) != 2) *tpc = *ks = -1;
 }
 
-// Fixed, shape-based plan (no autotuning).  Cost model: CTAs are spread over
-// the SMs; an SM streams its CTAs' weight slices at its share of HBM
-// bandwidth (capped per SM); each wave pays a fixed latency; split-K pays a
-// reduction; a CTA too big to share its SM with the next kernel's CTA (no
-// overlap under programmatic dependent launch) pays a penalty.
+// Fixed, shape-based plan (no autotuning).  The grid is persistent along N:
+// with more blocks than resident CTAs, each CTA runs R = ceil(blocks / CTAs)
+// blocks back to back while its producer keeps the ring full.  Cost model:
+// HBM bandwidth is shared by the active CTAs and limited by the bytes they
+// keep in flight (ring depth / latency) and by a per-SM cap; the decode
+// arithmetic is issue-bound at a fixed rate; the first data arrives after a
+// fixed latency; each block pays an epilogue and split-K a reduction.
 constexpr size_t kSmemShared = 110 * 1024;   // two CTAs per SM fit under this
 
-bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, GemvPlan* out) {
+bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, int scale_tma,
+               GemvPlan* out) {
   const int mt = M <= 8 ? 1 : 2;
   const int mc = 8 * mt;
   const int64_t kbytes = wbits == 4 ? K / 2 : K;
@@ -233,7 +254,15 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   const int x_rows = (int)std::min<int64_t>(mc, M);
   const int mchunks = (int)cdiv(M, mc);
   if (mchunks > 65535) return false;
-  const double bw_total = 6.5e12, bw_sm_max = 120e9, t_wave = 1.5e-6, t_red = 0.8e-6, t_big = 0.8e-6;
+  const int chunk = weight_chunk((uint64_t)kbytes);
+  if (chunk == 0) return false;
+  const int stma = wbits == 4 ? scale_tma : 0;
+  // model constants (B200): HBM bandwidth, loaded latency, per-SM stream
+  // cap, first-data latency, per-block epilogue, split-K reduction, and the
+  // decode issue cost (warp instructions per 2 KB k-block of one tile)
+  const double bw_total = 6.5e12, lat = 2.0e-6, bw_sm_max = 120e9, t_fill = 1.5e-6, t_blk = 0.25e-6,
+               t_red = 4.0e-6, issue_rate = 2.5 * 1.9e9, bw_x_sm = 60e9;
+  const double ipk = (wbits == 4 ? 250.0 : 170.0) * (mt == 2 ? 1.3 : 1.0);
   int o_tpc, o_ks;
   plan_override(&o_tpc, &o_ks);
 
@@ -261,52 +290,77 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       p.mchunks = mchunks;
       p.nblk = (int)nblk;
       p.nkb = nkb;
+      p.chunk = chunk;
+      p.scale_tma = stma;
       p.x_stride = kbps * epk + 8;
       p.x_rows = x_rows;
       p.wpt = std::min(kbps, ql::gemv::kMaxConsumerWarps / tpc);
       if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
       p.ws_bytes = gemv_ws_bytes(p);
       if (p.ws_bytes > ws_avail) continue;
-      // stages of one tile x kb_stage k-blocks, P ring slots per tile
-      // (stages = P * tpc): the whole slice resident if it fits next to a
-      // second CTA; else the fewest k-chunks that still double-buffer every
-      // tile; else single-k-block stages with whatever depth fits
-      const int chunk = weight_chunk((uint64_t)kbytes);
-      if (chunk == 0) continue;
       const ql::gemv::Smem base =
-          ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, 1, p.x_stride, kbps);
-      const size_t fixed = base.total - base.region0 + 2 * 8 * 64;
-      bool placed = false;
-      for (size_t budget : {kSmemShared, kSmemOptin}) {
+          ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, 0, 1, p.x_stride, kbps, stma);
+      const size_t fixed = base.total + 2 * 8 * 64;
+      const double per_x = (double)ks_eff * mchunks;   // CTAs per block column
+      for (int per_sm : {2, 1}) {
+        const size_t budget = per_sm == 2 ? kSmemShared : kSmemOptin;
         if (budget <= fixed) continue;
-        for (int nkc = 1; nkc <= kbps && !placed; ++nkc) {
-          const int kbs = (int)cdiv(kbps, nkc);
-          if (kbs * 128 / chunk > 256) continue;
-          const size_t stage_bytes = (size_t)16 * kbs * 128;
+        // blocks per CTA and grid width
+        const double slots_x = std::max(1.0, std::floor((double)sms * per_sm / per_x));
+        const int64_t R = cdiv(nblk, (int64_t)slots_x);
+        const int64_t gx = cdiv(nblk, R);
+        // stages: the largest k-chunk that still leaves every tile at least
+        // two ring slots (one when a tile has a single stage in total)
+        int kbs = 0, P = 0;
+        for (int nkc = 1; nkc <= kbps; ++nkc) {
+          const int kb = (int)cdiv(kbps, nkc);
+          if (kb * 128 / chunk > 256 || (stma && 2 * kb > 256)) continue;   // TMA box extents
+          const int nkc_eff = (int)cdiv(kbps, kb);
+          const size_t stage_bytes =
+              ql::gemv::stage_weight_bytes(kb) + ql::gemv::stage_scale_bytes(wbits, stma, kb);
           const int fit = (int)std::min<size_t>(64, (budget - fixed) / stage_bytes);
-          const int per_tile = std::min(nkc, fit / tpc);
-          if (per_tile == nkc || (nkc > 1 && per_tile >= 2) || (nkc == kbps && per_tile >= 1)) {
-            p.kb_stage = kbs;
-            p.stages = per_tile * tpc;
-            placed = true;
+          const int64_t per_tile_total = (int64_t)nkc_eff * R;
+          const int Pc = (int)std::min<int64_t>(std::min(fit / tpc, 16), per_tile_total);
+          if (Pc >= std::min<int64_t>(2, per_tile_total)) {
+            kbs = kb;
+            P = Pc;
+            break;
           }
         }
-        if (placed) break;
-      }
-      if (!placed) continue;
-      p.chunk = chunk;
-      p.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, p.wpt, p.stages, p.kb_stage, p.x_stride, kbps).total;
-      if (p.smem > kSmemOptin) continue;
-      const double ctas = (double)nblk * ks_eff * mchunks;
-      const double waves = std::ceil(ctas / sms);
-      const double active = std::min<double>(ctas, sms);
-      const double cta_bytes = (double)tpc * 16 * kbps * 128;
-      const double bw_sm = std::min(bw_total / active, bw_sm_max);
-      p.cost = waves * (cta_bytes / bw_sm + t_wave) + (ks_eff > 1 ? t_red : 0.0) +
-               (p.smem > kSmemShared ? t_big : 0.0);
-      if (p.cost < best.cost * 0.999) {
-        best = p;
-        found = true;
+        if (P == 0) continue;
+        GemvPlan q = p;
+        q.kb_stage = kbs;
+        q.stages = P * tpc;
+        q.gx = (int)gx;
+        q.smem = ql::gemv::smem_layout(wbits, mc, x_rows, tpc, q.wpt, q.stages, kbs, q.x_stride, kbps, stma).total;
+        if (q.smem > kSmemOptin) continue;
+        const int resident = q.smem <= kSmemShared ? 2 : 1;
+        const double ctas = (double)gx * per_x;
+        const double active = std::min(ctas, (double)sms * resident);
+        const double stage_b = (double)(16 * kbs * 128);
+        const double inflight = active * std::max(1, P - 1) * tpc * stage_b;
+        const double bw = std::min(bw_total, inflight / lat);
+        const double bw_cta = std::min(bw / active, bw_sm_max / resident);
+        // weights of the CTA's blocks, its x slice (staged once, from L2 at a
+        // per-SM rate) and, with split-K, the fp32 partials written and read
+        const double bytes_cta = (double)R * tpc * 16 * kbps * 128 +
+                                 (ks_eff > 1 ? (double)R * mc * tpc * 16 * 4 * 2.0 : 0.0);
+        const double x_cta = (double)x_rows * kbps * epk * 2;
+        const double t_mem = bytes_cta / bw_cta + x_cta / bw_x_sm;
+        const double tiles_kb = (double)NT * nkb * mchunks;   // 2 KB units, all CTAs
+        const double t_comp = tiles_kb * ipk / (std::min<double>(ctas, sms) * issue_rate);
+        q.cost = t_fill + std::max(t_mem, t_comp) + R * t_blk + (ks_eff > 1 ? t_red : 0.0);
+        // measured on B200: a warp should own 3..8 k-blocks of a tile's split
+        // (fewer: the block epilogue dominates; more: the tile's stages drain
+        // too slowly to keep its ring slots turning over)
+        const double kb_per_warp = (double)kbps / q.wpt;
+        if (kb_per_warp < 3.0) q.cost *= 1.0 + 0.1 * (3.0 - kb_per_warp);
+        if (kb_per_warp > 8.0) q.cost *= 1.0 + 0.03 * (kb_per_warp - 8.0);
+        if (tpc == 8) q.cost *= 1.4;   // measured: 8-tile blocks are always slower than 4-tile ones
+        if (q.cost < best.cost * 0.999) {
+          best = q;
+          found = true;
+        }
       }
     }
   }
@@ -315,15 +369,15 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
 }
 
 template <int WBITS, int LAYOUT, int MT>
-int launch_gemv_t(const GemvPlan& pl, const CUtensorMap& tm, const ql::gemv::Params& prm, cudaStream_t s,
-                  bool pdl) {
+int launch_gemv_t(const GemvPlan& pl, const CUtensorMap& tm, const CUtensorMap& tms, const ql::gemv::Params& prm,
+                  cudaStream_t s, bool pdl) {
   auto kern = ql::gemv::qgemv_kernel<WBITS, LAYOUT, MT>;
   const int slot = (WBITS == 4 ? 0 : 8) + LAYOUT * 4 + MT;
   int st = allow_smem(kern, slot);
   if (st != QL_OK) return st;
-  dim3 grid(pl.nblk, pl.ks, pl.mchunks);
+  dim3 grid(pl.gx, pl.ks, pl.mchunks);
   dim3 block((pl.tpc * pl.wpt + 1) * 32);
-  return launch(kern, grid, block, pl.smem, s, pdl, tm, prm);
+  return launch(kern, grid, block, pl.smem, s, pdl, tm, tms, prm);
 }
 
 struct LinearArgs {
@@ -371,14 +425,23 @@ int run_generic(const LinearArgs& a);
 int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   GemvPlan pl;
   const size_t avail = a.ws ? a.ws_bytes : 0;
+  // int4 scales travel with the weight stages (TMA) when their rows are
+  // 16-byte aligned; otherwise every block stages them with plain loads
+  const int scale_tma = (a.wbits == 4 && aligned16(a.scale) && a.lds % 8 == 0) ? 1 : 0;
   // no decode plan fits (e.g. a tall K with many batch rows and no
   // workspace for split-K): the portable kernel takes it
-  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, &pl)) return run_generic(a);
-  if (pl.stages < pl.tpc || pl.stages % pl.tpc != 0) return QL_ERR_UNSUPPORTED;   // per-tile ring slots
-  CUtensorMap tm;
+  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, scale_tma, &pl)) return run_generic(a);
+  if (pl.stages < pl.tpc || pl.stages % pl.tpc != 0 || pl.gx < 1 || pl.gx > pl.nblk)
+    return QL_ERR_UNSUPPORTED;
+  CUtensorMap tm, tms;
+  std::memset(&tms, 0, sizeof(tms));
   const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   int st = make_weight_map(&tm, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, pl.chunk, pl.kb_stage);
   if (st != QL_OK) return st;
+  if (pl.scale_tma) {
+    st = make_scale_map(&tms, a.scale, (uint64_t)a.N, (uint64_t)(a.K / 128), (uint64_t)a.lds, pl.kb_stage);
+    if (st != QL_OK) return st;
+  }
   ql::gemv::Params p;
   p.x = static_cast<const __half*>(a.x);
   p.scale = a.scale;
@@ -401,6 +464,8 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   p.chunk = pl.chunk;
   p.x_stride = pl.x_stride;
   p.x_rows = pl.x_rows;
+  p.nblk = pl.nblk;
+  p.scale_tma = pl.scale_tma;
   p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
   p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
   const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
@@ -415,14 +480,14 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
     p.partials = nullptr;
   }
   if (a.wbits == 8) {
-    return pl.mt == 1 ? launch_gemv_t<8, 0, 1>(pl, tm, p, a.stream, pdl)
-                      : launch_gemv_t<8, 0, 2>(pl, tm, p, a.stream, pdl);
+    return pl.mt == 1 ? launch_gemv_t<8, 0, 1>(pl, tm, tms, p, a.stream, pdl)
+                      : launch_gemv_t<8, 0, 2>(pl, tm, tms, p, a.stream, pdl);
   }
   if (a.layout == QL_W4_LAYOUT_SPLIT_HALF)
-    return pl.mt == 1 ? launch_gemv_t<4, 0, 1>(pl, tm, p, a.stream, pdl)
-                      : launch_gemv_t<4, 0, 2>(pl, tm, p, a.stream, pdl);
-  return pl.mt == 1 ? launch_gemv_t<4, 1, 1>(pl, tm, p, a.stream, pdl)
-                    : launch_gemv_t<4, 1, 2>(pl, tm, p, a.stream, pdl);
+    return pl.mt == 1 ? launch_gemv_t<4, 0, 1>(pl, tm, tms, p, a.stream, pdl)
+                      : launch_gemv_t<4, 0, 2>(pl, tm, tms, p, a.stream, pdl);
+  return pl.mt == 1 ? launch_gemv_t<4, 1, 1>(pl, tm, tms, p, a.stream, pdl)
+                    : launch_gemv_t<4, 1, 2>(pl, tm, tms, p, a.stream, pdl);
 }
 
 template <int WBITS, int LAYOUT, int BN>
@@ -560,9 +625,13 @@ static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
   int st;
   DeviceInfo* dev = current_device(&st);
   if (!dev) return 0;
-  GemvPlan pl;
-  if (!plan_gemv(wbits, M, N, K, dev->sms, SIZE_MAX, &pl)) return 0;
-  return pl.ws_bytes;
+  // the larger of the two int4 scale paths, so a buffer of this size serves both
+  size_t bytes = 0;
+  for (int stma : {0, 1}) {
+    GemvPlan pl;
+    if (plan_gemv(wbits, M, N, K, dev->sms, SIZE_MAX, stma, &pl)) bytes = std::max(bytes, pl.ws_bytes);
+  }
+  return bytes;
 }
 
 size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(8, M, N, K); }
@@ -576,9 +645,9 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
   DeviceInfo* dev = current_device(&st);
   const int sms = dev ? dev->sms : 148;   // without a device: the B200 SM count
   GemvPlan pl;
-  if (!plan_gemv(wbits, M, N, K, sms, workspace_bytes, &pl)) return QL_ERR_UNSUPPORTED;
+  if (!plan_gemv(wbits, M, N, K, sms, workspace_bytes, 1, &pl)) return QL_ERR_UNSUPPORTED;
   const int64_t v[12] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
-                         (int64_t)pl.nblk * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes,
+                         (int64_t)pl.gx * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes,
                          pl.kb_stage, pl.chunk};
   for (int i = 0; i < 12; ++i) fields[i] = v[i];
   return QL_OK;

@@ -241,7 +241,11 @@ def test_multiwave_ring_reuse_repeated(K, N, M):
     w_q, scale = w8a16_quantize_cuda(w)
     del w
     plan = _lib.gemv_plan(8, M, N, K)
-    assert plan["stages"] < plan["tiles_per_cta"] * plan["kblocks_per_split"] // plan["kblocks_per_stage"]
+    # the per-tile rings wrap: fewer slots than the stages a CTA streams
+    blocks = -(-(-(-N // 16)) // plan["tiles_per_cta"])
+    per_cta = -(-blocks // (plan["ctas"] // (plan["k_splits"] * plan["batch_chunks"])))
+    stages_per_tile = -(-plan["kblocks_per_split"] // plan["kblocks_per_stage"]) * per_cta
+    assert plan["stages"] < plan["tiles_per_cta"] * stages_per_tile
     x = make_x(M, K, seed=K + 1).cuda()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
