@@ -43,9 +43,12 @@ struct Params {
   __half* out;            // [M, ldo]
   long long lds, ldo;
   int M, N, K;
-  int nk;                 // number of 128-k stages
+  int nk;                 // number of 128-k stages of K
+  int nk_split;           // stages per K-split (gridDim.z splits)
   int stages;             // shared-memory ring depth
   int scale_f32, bias_f32;
+  uint32_t* counters;     // [gridDim.y * gridDim.x] arrival counters (split-K)
+  float* partials;        // [gridDim.y * gridDim.x][gridDim.z][BN][128] fp32 (split-K)
   unsigned* err;
 };
 
@@ -101,6 +104,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 8 consecutive fp32 accumulator columns of this thread's TMEM lane, waited.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+  tmem_ld_wait();
+}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), version 1.
@@ -136,11 +147,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dfull = afree + kASlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);   // a wait of this CTA gave up
+  volatile int* last_flag = abort + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
   const int m0 = blockIdx.y * BN;
-  const int nk = p.nk;
+  // this CTA's K-split: stages [kbeg, kbeg + nk)
+  const int kbeg = blockIdx.z * p.nk_split;
+  const int nk = min(p.nk - kbeg, p.nk_split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -185,9 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* st = smem + (size_t)s * L::kStage;
         mbar_arrive_expect_tx(full + s, L::kTx);
-        tma_load_2d(smem_u32(st), &tmap_x, i * kBK, m0, full + s, pol_x);
-        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, i * kBK + 64, m0, full + s, pol_x);
-        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, i, n0, full + s, pol_w);
+        tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, full + s, pol_x);
+        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, full + s, pol_x);
+        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, full + s, pol_w);
         issued = i + 1;
       }
       // every issued copy lands before the CTA can exit (only the last
@@ -234,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const __half* sc4 = static_cast<const __half*>(p.scale);
     // int4 group scale of this row for stage i (0 past N), two stages ahead
     auto load_scale = [&](int i) -> __half {
-      return (WBITS == 4 && i < nk && n < p.N) ? sc4[(long long)i * p.lds + n] : __float2half(0.f);
+      return (WBITS == 4 && i < nk && n < p.N) ? sc4[(long long)(kbeg + i) * p.lds + n] : __float2half(0.f);
     };
     __half s_next = load_scale(0), s_next2 = load_scale(1);
     for (int i = 0; i < nk; ++i) {
@@ -254,21 +268,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (LAYOUT == 0) {
           // all 64 bytes of row r (64-byte swizzle: chunk q at q ^ ((r >> 1) & 3)); half 0 takes the
           // low nibbles (k = 4w..4w+3), half 1 the high nibbles (k = 64+4w..)
+          uint32_t wd[16];
           #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint4 v = lds128(wrow + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
-            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+            wd[4 * q] = v.x; wd[4 * q + 1] = v.y; wd[4 * q + 2] = v.z; wd[4 * q + 3] = v.w;
+          }
+          // the branch is per warp (uniform) and outside the unrolled loops
+          if (half == 0) {
             #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int w = 4 * q + e;
-              const uint32_t t0 = __byte_perm(wd[e], 0u, 0x1100), t1 = __byte_perm(wd[e], 0u, 0x3322);
-              if (half == 0) {
-                cols[2 * w] = h2_mul(h2_sub(lop3_and_or(t0, 0x000F000Fu, kH2Magic), kH2_1032), s2);
-                cols[2 * w + 1] = h2_mul(h2_sub(lop3_and_or(t1, 0x000F000Fu, kH2Magic), kH2_1032), s2);
-              } else {
-                cols[2 * w] = h2_mul(h2_fma(lop3_and_or(t0, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
-                cols[2 * w + 1] = h2_mul(h2_fma(lop3_and_or(t1, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
-              }
+            for (int w = 0; w < 16; ++w) {
+              const uint32_t t0 = __byte_perm(wd[w], 0u, 0x1100), t1 = __byte_perm(wd[w], 0u, 0x3322);
+              cols[2 * w] = h2_mul(h2_sub(lop3_and_or(t0, 0x000F000Fu, kH2Magic), kH2_1032), s2);
+              cols[2 * w + 1] = h2_mul(h2_sub(lop3_and_or(t1, 0x000F000Fu, kH2Magic), kH2_1032), s2);
+            }
+          } else {
+            #pragma unroll
+            for (int w = 0; w < 16; ++w) {
+              const uint32_t t0 = __byte_perm(wd[w], 0u, 0x1100), t1 = __byte_perm(wd[w], 0u, 0x3322);
+              cols[2 * w] = h2_mul(h2_fma(lop3_and_or(t0, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
+              cols[2 * w + 1] = h2_mul(h2_fma(lop3_and_or(t1, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72), s2);
             }
           }
         } else {
@@ -337,21 +356,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                         : __half2float(static_cast<const __half*>(p.bias)[n]);
     }
     constexpr int kHalfCols = BN / 2;
-    #pragma unroll 1
-    for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
-      uint32_t v[8];
-      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                   : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                     "=r"(v[7])
-                   : "r"(tmem + lane_base + (uint32_t)c0)
-                   : "memory");
-      tmem_ld_wait();
-      if (n < p.N) {
-        #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(__uint_as_float(v[j]), sc8, bv));
+    if (gridDim.z == 1) {
+      #pragma unroll 1
+      for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+        uint32_t v[8];
+        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        if (n < p.N) {
+          #pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(__uint_as_float(v[j]), sc8, bv));
+          }
         }
+      }
+    } else {
+      // Split-K: every CTA of the tile stores its fp32 partial [BN][128] in
+      // its own slot; the last to arrive sums the slots in split order,
+      // applies scale and bias, and zeroes its slots and the counter again.
+      const size_t tile_id = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+      constexpr int kSlot = BN * kTileN;
+      float* slots = p.partials + tile_id * gridDim.z * kSlot;
+      float* mine = slots + (size_t)blockIdx.z * kSlot;
+      #pragma unroll 1
+      for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+        uint32_t v[8];
+        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) mine[(c0 + j) * kTileN + r] = __uint_as_float(v[j]);
+      }
+      named_bar_sync(1, 256);                       // the 8 epilogue warps
+      if (threadIdx.x == 64) {
+        // one thread releases the CTA's partials (cumulative over the
+        // barrier) and, if it arrives last, acquires the other splits'
+        __threadfence();
+        const unsigned old = atomicAdd(p.counters + tile_id, 1u);
+        const int last = old == gridDim.z - 1;
+        if (last) __threadfence();
+        *last_flag = last;
+      }
+      named_bar_sync(1, 256);
+      if (*last_flag) {
+        #pragma unroll 1
+        for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; ++c) {
+          float acc = 0.f;
+          for (unsigned z = 0; z < gridDim.z; ++z) {
+            float* slot = slots + (size_t)z * kSlot + c * kTileN + r;
+            acc += __ldcg(slot);
+            __stcg(slot, 0.f);                      // leave the workspace zeroed
+          }
+          const int m = m0 + c;
+          if (n < p.N && m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(acc, sc8, bv));
+        }
+        if (threadIdx.x == 64) p.counters[tile_id] = 0u;
       }
     }
   }

@@ -526,15 +526,18 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
           mine[idx] = v;
         }
       }
-      __threadfence();
       named_bar_sync(1, nct);
       if (ctid == 0) {
+        // one thread releases the CTA's partials (the fence is cumulative over
+        // the barrier) and, if it arrives last, acquires the other splits'
+        __threadfence();
         const unsigned old = atomicAdd(p.counters + tile_id, 1u);
-        *last_flag = (old == (unsigned)(p.ks - 1));
+        const int last = old == (unsigned)(p.ks - 1);
+        if (last) __threadfence();
+        *last_flag = last;
       }
       named_bar_sync(1, nct);
       if (*last_flag) {
-        __threadfence();
         for (int idx = ctid; idx < nout; idx += nct) {
           float v = 0.f;
           for (int s2 = 0; s2 < p.ks; ++s2) {

@@ -490,8 +490,45 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
                     : launch_gemv_t<4, 1, 2>(pl, tm, tms, p, a.stream, pdl);
 }
 
+// ------------------------------------------------------------- GEMM plan
+// Activation rows per CTA (int4 tiles at 256 when the batch fills them:
+// three 72 KB stages fit; int8 stays at 128), and a K-split that brings a
+// grid of fewer tiles than SMs up to about one CTA per SM (at least two
+// stages per split).  Split-K needs workspace; without enough, no split.
+struct GemmPlan {
+  int bn = 0, ks = 1, nk_split = 0;
+  int64_t tiles = 0;
+  size_t ws_bytes = 0, ws_counters = 0;
+};
+
+GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail) {
+  GemmPlan g;
+  g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : (M <= 128 || wbits == 8) ? 128 : 256;
+  g.tiles = cdiv(N, ql::gemm::kTileN) * cdiv(M, g.bn);
+  const int64_t nk = K / 128;
+  int64_t ks = 1;
+  if (g.tiles < sms) ks = std::max<int64_t>(1, std::min<int64_t>(nk / 2, sms / g.tiles));
+  for (; ks > 1; --ks) {
+    const int64_t per = cdiv(nk, ks);
+    const int64_t eff = cdiv(nk, per);
+    const size_t counters = ((size_t)g.tiles * 4 + 255) / 256 * 256;
+    const size_t bytes = counters + (size_t)g.tiles * eff * g.bn * ql::gemm::kTileN * 4;
+    if (eff <= 65535 && bytes <= ws_avail) {
+      g.ks = (int)eff;
+      g.nk_split = (int)per;
+      g.ws_counters = counters;
+      g.ws_bytes = bytes;
+      return g;
+    }
+  }
+  g.ks = 1;
+  g.nk_split = (int)nk;
+  return g;
+}
+
 template <int WBITS, int LAYOUT, int BN>
-int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm) {
+int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm,
+                  int ks) {
   using L = ql::gemm::Layout<WBITS, BN>;
   auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
   int S = (int)std::min<size_t>(6, (kSmemOptin - 1024 - 256) / L::kStage);
@@ -508,8 +545,8 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
     }
     done[dev].store(1, std::memory_order_release);
   }
-  dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN));
-  if (grid.y > 65535) return QL_ERR_BAD_SHAPE;
+  dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)ks);
+  if (grid.y > 65535 || grid.z > 65535) return QL_ERR_BAD_SHAPE;
   return launch(kern, grid, dim3(ql::gemm::kThreads), L::smem_bytes(S), a.stream, (a.flags & QL_FLAG_PDL) != 0,
                 tx, tw, prm);
 }
@@ -522,7 +559,8 @@ bool gemm_ok(const LinearArgs& a) {
 }
 
 template <int WBITS, int LAYOUT>
-int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, int bn) {
+int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
+  const int bn = g.bn;
   const uint64_t kbytes = WBITS == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   CUtensorMap tx, tw;
   int st = make_act_map(&tx, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx, bn);
@@ -539,30 +577,40 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, int bn) {
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.nk = (int)(a.K / 128);
+  p.nk_split = g.nk_split;
   p.stages = 0;
   p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
   p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  p.counters = g.ks > 1 ? static_cast<uint32_t*>(a.ws) : nullptr;
+  p.partials = g.ks > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + g.ws_counters) : nullptr;
   p.err = dev->err_word;
   switch (bn) {
-    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p);
-    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p);
-    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p);
-    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p);
-    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 128>(a, tx, tw, p);
+    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.ks);
+    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.ks);
+    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.ks);
+    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.ks);
+    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 128>(a, tx, tw, p, g.ks);
   }
 }
 
 int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
-  // activation rows per CTA; int4 tiles at 256 when the batch fills them
-  // (three 72 KB stages fit), int8 stays at 128 (four 80 KB stages would not)
-  const int bn = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : (a.M <= 128 || a.wbits == 8) ? 128 : 256;
-  if (a.wbits == 8) return run_gemm_layout<8, 0>(a, dev, bn);
-  if (a.layout == QL_W4_LAYOUT_SPLIT_HALF) return run_gemm_layout<4, 0>(a, dev, bn);
-  return run_gemm_layout<4, 1>(a, dev, bn);
+  const GemmPlan g = plan_gemm(a.wbits, a.M, a.N, a.K, dev->sms, a.ws ? a.ws_bytes : 0);
+  if (a.wbits == 8) return run_gemm_layout<8, 0>(a, dev, g);
+  if (a.layout == QL_W4_LAYOUT_SPLIT_HALF) return run_gemm_layout<4, 0>(a, dev, g);
+  return run_gemm_layout<4, 1>(a, dev, g);
 }
 
-// Batch size from which the tensor-core GEMM replaces the decode kernel.
+// Where the tensor-core GEMM replaces the decode kernel (measured on B200):
+// from 65 batch rows always; on wide layers (lm_head, fused MLP
+// projections) from 16 rows, and from 8 when K is long too — there
+// decoding the weights once for the whole batch beats the decode kernel's
+// larger activation slice per CTA.
 constexpr int64_t kGemmMinM = 65;
+constexpr int64_t kWideN = 12288;
+bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
+  (void)wbits;
+  return M >= kGemmMinM || (N >= kWideN && (M >= 16 || (M >= 8 && K >= 4096)));
+}
 
 int run_linear(const LinearArgs& a) {
   if (!a.x || !a.w || !a.scale || !a.out) {
@@ -591,7 +639,7 @@ int run_linear(const LinearArgs& a) {
     return run_gemm(a, dev);
   }
   if ((a.flags & QL_FLAG_FORCE_GENERIC) || !fast_ok) return run_generic(a);
-  if (!(a.flags & QL_FLAG_FORCE_GEMV) && a.M >= kGemmMinM && gemm_ok(a)) return run_gemm(a, dev);
+  if (!(a.flags & QL_FLAG_FORCE_GEMV) && use_gemm(a.wbits, a.M, a.N, a.K) && gemm_ok(a)) return run_gemm(a, dev);
   return run_gemv(a, dev);
 }
 
@@ -625,7 +673,10 @@ static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
   int st;
   DeviceInfo* dev = current_device(&st);
   if (!dev) return 0;
-  // the larger of the two int4 scale paths, so a buffer of this size serves both
+  // enough for the kernel the dispatch picks; for the decode kernel, the
+  // larger of its two int4 scale paths (a forced tensor-core call with less
+  // workspace than its split-K needs simply runs unsplit)
+  if (K % 128 == 0 && use_gemm(wbits, M, N, K)) return plan_gemm(wbits, M, N, K, dev->sms, SIZE_MAX).ws_bytes;
   size_t bytes = 0;
   for (int stma : {0, 1}) {
     GemvPlan pl;

@@ -22,8 +22,9 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="requires a CUDA GPU")]
 
 
-def _call(x, q, flags):
+def _call(x, q, flags, ws=None):
     lib = _lib.load()
+    wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     dev = x.device
     stream = torch.cuda.current_stream(dev).cuda_stream
     if isinstance(q, QuantizedLinearInt4):
@@ -34,7 +35,7 @@ def _call(x, q, flags):
             x.data_ptr(), 0, q.weight_packed.data_ptr(), q.layout, q.scales.data_ptr(),
             q.bias.data_ptr() if q.bias is not None else None, 0,
             out.data_ptr(), x.shape[0], N, K, _launch.ld(x, K), _launch.ld(q.weight_packed, K // 2),
-            _launch.ld(q.scales, N), _launch.ld(out, N), None, 0, flags, stream)
+            _launch.ld(q.scales, N), _launch.ld(out, N), wsp, wsn, flags, stream)
     else:
         N, K = q.weight_q.shape
         out = torch.empty((x.shape[0], N), dtype=torch.float16, device=dev)
@@ -42,7 +43,7 @@ def _call(x, q, flags):
             x.data_ptr(), 0, q.weight_q.data_ptr(), q.scale.data_ptr(), _launch.dtype_code(q.scale.dtype),
             q.bias.data_ptr() if q.bias is not None else None, 0,
             out.data_ptr(), x.shape[0], N, K, _launch.ld(x, K), _launch.ld(q.weight_q, K), _launch.ld(out, N),
-            None, 0, flags, stream)
+            wsp, wsn, flags, stream)
     _lib.check(st)
     return out
 
@@ -109,6 +110,30 @@ def test_gemm_unsupported_shape_is_reported():
     # the default dispatch handles it (decode kernel), correctly
     y32, deq = _oracle8(x, q)
     assert_parity(q(x), y32, x.cpu().numpy(), deq, "k144 default")
+
+
+@pytest.mark.parametrize("K,N", [(8960, 1536), (1536, 8960), (4096, 256), (2048, 1000)])
+@pytest.mark.parametrize("M", [1, 16, 33, 64, 200])
+@pytest.mark.parametrize("wbits", [4, 8])
+def test_gemm_split_k(K, N, M, wbits):
+    """Grids with fewer tiles than SMs split K across CTAs (workspace given):
+    parity, bit-identical repeat, workspace left zeroed."""
+    lin = make_linear(K, N, bias=True, std=0.02, seed=K + N + M + wbits)
+    x = make_x(M, K, seed=M + 11)
+    if wbits == 4:
+        q = QuantizedLinearInt4.from_linear(lin)
+        y32, deq = _oracle4(x, q)
+    else:
+        q = QuantizedLinearInt8.from_linear(lin)
+        y32, deq = _oracle8(x, q)
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")   # room for any split
+    qd, xd = q.cuda(), x.cuda()
+    a = _call(xd, qd, _lib.QL_FLAG_FORCE_GEMM, ws)
+    b = _call(xd, qd, _lib.QL_FLAG_FORCE_GEMM | _lib.QL_FLAG_PDL, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert int(ws.count_nonzero()) == 0
+    assert_parity(a, y32, x.numpy(), deq, f"split-K w{wbits} K{K} N{N} M{M}")
 
 
 def test_gemm_no_device_error():
