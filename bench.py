@@ -636,11 +636,29 @@ def run_profile_one(args):
         layers.append(w4a16_quantize_cuda(w) if wbits == 4 else w8a16_quantize_cuda(w))
         del w
     x = torch.randn(M, K, generator=gen, device=dev).half()
-    for i in range(args.steps):
-        a, b = layers[i % copies]
-        (w4a16_linear if wbits == 4 else w8a16_linear)(x, a, b)
+    if args.path == "auto":
+        for i in range(args.steps):
+            a, b = layers[i % copies]
+            (w4a16_linear if wbits == 4 else w8a16_linear)(x, a, b)
+    else:
+        # one kernel family forced through the C ABI (its split-K workspace included)
+        from qlinear import _lib
+        lib = _lib.load()
+        flag = (_lib.QL_FLAG_FORCE_GEMM if args.path == "gemm" else _lib.QL_FLAG_FORCE_GEMV) | _lib.QL_FLAG_PDL
+        out = torch.empty(M, N, dtype=torch.float16, device=dev)
+        ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for i in range(args.steps):
+            a, b = layers[i % copies]
+            if wbits == 4:
+                st = lib.ql_w4a16_linear(x.data_ptr(), 0, a.data_ptr(), 0, b.data_ptr(), None, 0, out.data_ptr(),
+                                         M, N, K, K, K // 2, N, N, ws.data_ptr(), ws.numel(), flag, stream)
+            else:
+                st = lib.ql_w8a16_linear(x.data_ptr(), 0, a.data_ptr(), b.data_ptr(), 1, None, 0, out.data_ptr(),
+                                         M, N, K, K, K, N, ws.data_ptr(), ws.numel(), flag, stream)
+            _lib.check(st)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_one": args.profile_one, "launches": args.steps, "copies": copies}))
+    print(json.dumps({"profile_one": args.profile_one, "path": args.path, "launches": args.steps, "copies": copies}))
     return 0
 
 
@@ -655,6 +673,8 @@ def main():
     ap.add_argument("--workload", choices=("config1", "prefill", "sharded"), default="config1")
     ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
                     help="a few eager launches of one layer shape (small case for ncu)")
+    ap.add_argument("--path", choices=("auto", "gemv", "gemm"), default="auto",
+                    help="with --profile-one: force the decode or the tensor-core kernel")
     args = ap.parse_args()
     if args.profile_one:
         return run_profile_one(args)

@@ -396,16 +396,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_bar_sync(1, 256);
       if (*last_flag) {
+        // 8 columns at a time: the 8 loads of a split are independent, so
+        // each split costs one L2 round trip per chunk (sums stay in split order)
         #pragma unroll 1
-        for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; ++c) {
-          float acc = 0.f;
+        for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          #pragma unroll 1
           for (unsigned z = 0; z < gridDim.z; ++z) {
-            float* slot = slots + (size_t)z * kSlot + c * kTileN + r;
-            acc += __ldcg(slot);
-            __stcg(slot, 0.f);                      // leave the workspace zeroed
+            const float* sl = slots + (size_t)z * kSlot + (size_t)c0 * kTileN + r;
+            float t[8];
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) t[j] = __ldcg(sl + j * kTileN);
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += t[j];
           }
-          const int m = m0 + c;
-          if (n < p.N && m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(acc, sc8, bv));
+          #pragma unroll 1
+          for (unsigned z = 0; z < gridDim.z; ++z) {   // leave the workspace zeroed
+            float* sl = slots + (size_t)z * kSlot + (size_t)c0 * kTileN + r;
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) __stcg(sl + j * kTileN, 0.f);
+          }
+          if (n < p.N) {
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = m0 + c0 + j;
+              if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(acc[j], sc8, bv));
+            }
+          }
         }
         if (threadIdx.x == 64) p.counters[tile_id] = 0u;
       }

@@ -539,12 +539,18 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       named_bar_sync(1, nct);
       if (*last_flag) {
         for (int idx = ctid; idx < nout; idx += nct) {
+          // slots in order, 8 independent loads in flight at a time
           float v = 0.f;
-          for (int s2 = 0; s2 < p.ks; ++s2) {
-            float* slot = slots + (size_t)s2 * slot_elems + idx;
-            v += __ldcg(slot);
-            __stcg(slot, 0.f);                       // leave the workspace zeroed
+          int s2 = 0;
+          for (; s2 + 8 <= p.ks; s2 += 8) {
+            float t[8];
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) t[j] = __ldcg(slots + (size_t)(s2 + j) * slot_elems + idx);
+            #pragma unroll
+            for (int j = 0; j < 8; ++j) v += t[j];
           }
+          for (; s2 < p.ks; ++s2) v += __ldcg(slots + (size_t)s2 * slot_elems + idx);
+          for (s2 = 0; s2 < p.ks; ++s2) __stcg(slots + (size_t)s2 * slot_elems + idx, 0.f);   // leave it zeroed
           const int m = idx >> rows_log2, r = idx & (rows_cta - 1);
           const int n = row0 + r;
           if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));

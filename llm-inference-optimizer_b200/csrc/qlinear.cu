@@ -349,7 +349,9 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
         const double t_mem = bytes_cta / bw_cta + x_cta / bw_x_sm;
         const double tiles_kb = (double)NT * nkb * mchunks;   // 2 KB units, all CTAs
         const double t_comp = tiles_kb * ipk / (std::min<double>(ctas, sms) * issue_rate);
-        q.cost = t_fill + std::max(t_mem, t_comp) + R * t_blk + (ks_eff > 1 ? t_red : 0.0);
+        // split-K: a reduction at the end, and per block an arrival round trip
+        // that stalls the CTA's consumers (measured ~2 us per block)
+        q.cost = t_fill + std::max(t_mem, t_comp) + R * t_blk + (ks_eff > 1 ? t_red + R * 2.0e-6 : 0.0);
         // measured on B200: a warp should own 3..8 k-blocks of a tile's split
         // (fewer: the block epilogue dominates; more: the tile's stages drain
         // too slowly to keep its ring slots turning over)
@@ -601,15 +603,16 @@ int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
 }
 
 // Where the tensor-core GEMM replaces the decode kernel (measured on B200):
-// from 65 batch rows always; on wide layers (lm_head, fused MLP
-// projections) from 16 rows, and from 8 when K is long too — there
-// decoding the weights once for the whole batch beats the decode kernel's
-// larger activation slice per CTA.
+// from 65 batch rows always, and from 16 on wide layers (lm_head, fused
+// MLP projections), where decoding the weights once for the whole batch
+// beats the decode kernel's two n8 batch tiles per CTA.
 constexpr int64_t kGemmMinM = 65;
+constexpr int64_t kGemmMinMWide = 16;
 constexpr int64_t kWideN = 12288;
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
   (void)wbits;
-  return M >= kGemmMinM || (N >= kWideN && (M >= 16 || (M >= 8 && K >= 4096)));
+  (void)K;
+  return M >= kGemmMinM || (M >= kGemmMinMWide && N >= kWideN);
 }
 
 int run_linear(const LinearArgs& a) {
