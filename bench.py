@@ -572,6 +572,7 @@ def run_sharded(args):
                     torch.cuda.synchronize(dev)
                     g_loc, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
                     g_col = torch.cuda.CUDAGraph() if world > 1 else None   # no exchange on one GPU
+                    g_arg = torch.cuda.CUDAGraph() if groups == 1 else None  # greedy head: argmax only
                     with torch.cuda.graph(g_loc, stream=stream):
                         sh.local_forward(x)
                     if g_col is not None:
@@ -579,19 +580,29 @@ def run_sharded(args):
                             sh.gather(y_loc)
                     with torch.cuda.graph(g_e2e, stream=stream):
                         sh(x)
+                    if g_arg is not None:
+                        sh.argmax(x)
+                        torch.cuda.synchronize(dev)
+                        with torch.cuda.graph(g_arg, stream=stream):
+                            sh.argmax(x)
                 t_loc, t_e2e = timed(g_loc), timed(g_e2e)
                 t_col = timed(g_col) if g_col is not None else 0.0
+                t_arg = timed(g_arg) if g_arg is not None else None
                 # graphs holding NCCL calls must be gone before the process group is destroyed
                 torch.cuda.synchronize(dev)
-                del g_loc, g_col, g_e2e
+                del g_loc, g_col, g_e2e, g_arg
                 if rank == 0:
                     print(f"[sharded] w{wbits} {name} M={M}: local {t_loc * 1e6:.1f} us, all-gather "
-                          f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us", file=sys.stderr, flush=True)
+                          f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us"
+                          + (f", argmax head {t_arg * 1e6:.1f} us" if t_arg is not None else ""),
+                          file=sys.stderr, flush=True)
                 lb = layer_bytes(wbits, K, N)
                 detail[f"w{wbits}_{name}_M{M}"] = {
                     "compute_us": round(t_loc * 1e6, 2), "allgather_us": round(t_col * 1e6, 2),
                     "e2e_us": round(t_e2e * 1e6, 2), "GBps_e2e": round(lb / t_e2e / 1e9, 1),
                     "GBps_compute_per_gpu": round(lb / world / t_loc / 1e9, 1)}
+                if t_arg is not None:
+                    detail[f"w{wbits}_{name}_M{M}"]["argmax_us"] = round(t_arg * 1e6, 2)
                 tot_bytes += lb
                 tot_s += t_e2e
             del sh, mod

@@ -194,6 +194,20 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
                       int qmin, int layout, uint8_t* w_packed, void* scales,
                       void* stream);
 
+/* ------------------------------------------------------------------ argmax */
+/* Row-wise argmax of fp16 logits x[M, ldx] (N columns) as packed keys:
+ *   keys[m] = max over n of (ord(x[m, n]) << 32) | (0xFFFFFFFF - (col_offset + n))
+ * with ord the order-preserving code of the fp16 bits, so the largest key is
+ * the largest logit and, among equal logits, the smallest column — the
+ * index torch.argmax returns.  Keys of column shards (each passing its first
+ * column as col_offset) combine with a max; column = 0xFFFFFFFF - low 32
+ * bits.  keys[M] (uint64, device) is overwritten.  Requires
+ * col_offset + N <= 2^32 - 1.  Replaces, for a sharded lm_head, the
+ * all-gather of the logits that the reference's greedy decode reduces with
+ * argmax (src/engine/paged_engine.py:146-147, graphed_decode_engine.py:114-115). */
+int ql_argmax_rows_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t col_offset,
+                       uint64_t* keys, void* stream);
+
 /* ------------------------------------------------------------- diagnostics */
 const char* ql_strerror(int status);
 /* Version as (major << 16) | (minor << 8) | patch. */

@@ -19,6 +19,7 @@
 
 #include "../../include/qlinear.h"
 #include "ql_common.cuh"
+#include "qargmax.cuh"
 #include "qformat.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
@@ -787,6 +788,27 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw, int qmin
                 dim3(128), 0,
                 static_cast<cudaStream_t>(stream), false, static_cast<const __half*>(w), (long long)ldw, (int)K,
                 qmin, layout, w_packed, static_cast<__half*>(scales), (int)N);
+}
+
+int ql_argmax_rows_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t col_offset, uint64_t* keys,
+                       void* stream) {
+  if (M == 0) return QL_OK;
+  if (!x || !keys) return QL_ERR_NULL_POINTER;
+  if (M < 0 || N <= 0 || M > 65535 || N > INT_MAX || col_offset < 0 || col_offset + N > 0xFFFFFFFFLL)
+    return QL_ERR_BAD_SHAPE;
+  if (ldx < N) return QL_ERR_BAD_STRIDE;
+  int st;
+  if (!current_device(&st)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(keys, 0, (size_t)M * sizeof(uint64_t), s) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  const int vec = aligned16(x) && ldx % 8 == 0 && N % 8 == 0;
+  const int span = 8192;   // columns per CTA
+  return launch(ql::amax::argmax_rows_kernel, dim3((unsigned)cdiv(N, span), (unsigned)M), dim3(256), 0, s, false,
+                static_cast<const __half*>(x), (long long)ldx, (int)N, span, (long long)col_offset, vec,
+                reinterpret_cast<unsigned long long*>(keys));
 }
 
 // Once per device, with that device current: the host-side name of

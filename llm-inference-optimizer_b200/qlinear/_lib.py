@@ -62,6 +62,7 @@ SIGNATURES = {
     "ql_w4a16_unpack": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "ql_w8a16_quantize": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "ql_w4a16_quantize": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp]),
+    "ql_argmax_rows_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "ql_strerror": (ctypes.c_char_p, [_int]),
     "ql_version": (_int, []),
     "ql_device_error": (_int, [ctypes.POINTER(_int)]),

@@ -25,6 +25,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from .kernels.argmax import argmax_keys, combine_keys, key_columns
 from .kernels.w4a16_matmul import GROUP_SIZE, w4a16_linear
 from .kernels.w8a16_matmul import w8a16_linear
 from .quantization.int4 import QuantizedLinearInt4
@@ -68,7 +69,8 @@ class ShardedQuantizedLinear(nn.Module):
 
     def __init__(self, local: nn.Module, out_features: int, rank: int, world: int, groups: int = 1,
                  group: Optional[dist.ProcessGroup] = None,
-                 local_fn: Callable[[nn.Module, torch.Tensor], torch.Tensor] = local_linear_cuda):
+                 local_fn: Callable[[nn.Module, torch.Tensor], torch.Tensor] = local_linear_cuda,
+                 key_fn: Callable[[torch.Tensor, int], torch.Tensor] = argmax_keys):
         super().__init__()
         self.local = local
         self.out_features = out_features
@@ -76,6 +78,7 @@ class ShardedQuantizedLinear(nn.Module):
         self.rank, self.world, self.groups = rank, world, groups
         self.group = group
         self.local_fn = local_fn
+        self.key_fn = key_fn
         n = out_features // groups
         self.block = (n + world - 1) // world          # padded per-rank width of one group
         self.widths = [shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0] for r in range(world)]
@@ -146,6 +149,25 @@ class ShardedQuantizedLinear(nn.Module):
         n = self.out_features // self.groups
         full = full.reshape(M, self.groups, self.world * self.block)[:, :, :n]
         return full.reshape(M, self.out_features)
+
+    def argmax(self, x: torch.Tensor) -> torch.Tensor:
+        """argmax over the full output row, without gathering the outputs.
+
+        Each rank reduces its columns to one key per row (value, global
+        column; ties to the smallest column, as torch.argmax), the ranks
+        all-gather the keys (8 bytes per row and rank) and every rank takes
+        the max.  Equals torch.argmax(self(x), dim=-1).  groups == 1 only."""
+        assert self.groups == 1, "argmax is defined for a single output block"
+        K = self.in_features
+        x2 = x.reshape(-1, K)
+        y = self.local_fn(self.local, x2)                       # [M, widths[rank]]
+        lo = shard_bounds(self.out_features, self.rank, self.world)[0]
+        keys = self.key_fn(y, lo)                               # [M] int64 key bits
+        if self.world > 1:
+            buf = torch.empty(self.world * keys.numel(), dtype=keys.dtype, device=keys.device)
+            dist.all_gather_into_tensor(buf, keys, group=self.group)
+            keys = combine_keys(buf.view(self.world, -1), dim=0)
+        return key_columns(keys).reshape(x.shape[:-1])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         K = self.in_features

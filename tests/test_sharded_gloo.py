@@ -35,6 +35,16 @@ def _oracle_local(module, x2):
     return torch.from_numpy(orc.linear_f32(x2.numpy(), deq, b).astype(np.float16))
 
 
+def _cpu_keys(y, col_offset):
+    """Checker restatement of the argmax key (value order, then smallest column)."""
+    bits = y.contiguous().view(torch.int16).to(torch.int64) & 0xFFFF
+    bits = torch.where(bits == 0x8000, torch.zeros_like(bits), bits)
+    bits = torch.where((bits & 0x7FFF) > 0x7C00, torch.full_like(bits, 0x7FFF), bits)
+    ordv = torch.where(bits >= 0x8000, 0xFFFF - bits, bits | 0x8000)
+    cols = torch.arange(y.shape[1], dtype=torch.int64) + col_offset
+    return ((ordv << 32) | (0xFFFFFFFF - cols)).amax(dim=1)
+
+
 def _full_layer(K, N, wbits, seed):
     from qlinear.quantization.int4 import QuantizedLinearInt4
     from qlinear.quantization.int8 import QuantizedLinearInt8
@@ -55,14 +65,31 @@ def _worker(rank, world, port, case, result_q):
                                 timeout=datetime.timedelta(seconds=20))
         K, N, M, wbits, groups, mode = case
         lin, q = _full_layer(K, N, wbits, seed=7)
+        if mode == "tie":
+            # columns 5 and N-3 hold the same weights and the largest bias: the
+            # argmax is the smaller column on every row
+            from qlinear.quantization.int4 import QuantizedLinearInt4
+            from qlinear.quantization.int8 import QuantizedLinearInt8
+            with torch.no_grad():
+                lin.weight[N - 3].copy_(lin.weight[5])
+                lin.bias[5] = lin.bias[N - 3] = 30.0
+            q = QuantizedLinearInt4.from_linear(lin) if wbits == 4 else QuantizedLinearInt8.from_linear(lin)
         if mode == "from_linear":
             sh = ShardedQuantizedLinear.from_linear(lin, wbits, rank, world, groups=groups, local_fn=_oracle_local)
         else:
-            sh = ShardedQuantizedLinear.from_quantized(q, rank, world, groups=groups, local_fn=_oracle_local)
+            sh = ShardedQuantizedLinear.from_quantized(q, rank, world, groups=groups, local_fn=_oracle_local,
+                                                       key_fn=_cpu_keys)
         g = torch.Generator().manual_seed(11)
         x = torch.randn(M, K, generator=g).half()
         if mode == "die" and rank == 1:
             os._exit(3)                                   # leaves before the collective
+        if mode in ("argmax", "tie"):
+            idx = sh.argmax(x)
+            want = torch.argmax(_oracle_local(q, x), dim=-1)
+            ok = torch.equal(idx, want) and (mode != "tie" or bool((idx == 5).all()))
+            result_q.put((rank, "ok" if ok else "mismatch", f"{idx.tolist()} vs {want.tolist()}"))
+            dist.destroy_process_group()
+            return
         try:
             y = sh(x)
         except Exception as e:                            # the surviving rank must see an error
@@ -101,6 +128,20 @@ def _run(world, case, timeout=120):
     (2, (256, 512, 1, 4, 2, "from_linear")),        # shard-then-quantize == quantize-then-shard
 ])
 def test_sharded_matches_full_layer(world, case):
+    res, codes = _run(world, case)
+    assert len(res) == world, (res, codes)
+    for rank, status, info in res:
+        assert status == "ok", (rank, status, info)
+
+
+@pytest.mark.parametrize("world,case", [
+    (2, (256, 301, 6, 4, 1, "argmax")),             # uneven shards, int4
+    (4, (128, 1003, 3, 8, 1, "argmax")),            # 4 ranks, int8
+    (2, (256, 300, 4, 4, 1, "tie")),                # equal maxima in different shards -> smaller column
+])
+def test_sharded_argmax_matches_full_layer(world, case):
+    """argmax through per-rank keys + all-gather of keys == argmax of the
+    full layer's logits (ties to the smallest column, as torch.argmax)."""
     res, codes = _run(world, case)
     assert len(res) == world, (res, codes)
     for rank, status, info in res:
