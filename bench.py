@@ -502,17 +502,24 @@ def layer_bytes(wbits, K, N):
 def run_sharded(args):
     """`--workload sharded`: BASELINE config 4.  Every rank holds its column
     shard of each layer (quantized on the device), runs the local kernel and
-    one NCCL all-gather of the fp16 outputs.  Per (wbits, layer, M), three
-    CUDA graphs are timed: local compute only, the all-gather only, and the
-    whole sharded forward; L2 is flushed before every timed replay and the
-    reported time is the max over ranks of each rank's median.  value =
-    total weight bytes of all layers / total end-to-end time (strong
-    scaling: the same layers at every GPU count)."""
+    one NCCL all-gather of the fp16 outputs; for the lm_heads the greedy
+    head (argmax only) also runs as one kernel per rank that exchanges the
+    per-row argmax keys over NVLink (qlinear.p2p).  Per (wbits, layer, M),
+    CUDA graphs of R back-to-back iterations are timed — local compute only,
+    the all-gather only, the whole sharded forward, the argmax head — each
+    iteration on the next of C distinct weight copies (C x shard bytes >
+    2 x L2, so no iteration finds its weights in L2, and rank skew is paid
+    once per R iterations, as in a steady decode loop).  Time per iteration
+    = graph time / R, max over ranks.  value = total weight bytes of all
+    layers / total end-to-end time (strong scaling: the same layers at
+    every GPU count)."""
     import datetime
+    import math
     import torch
     import torch.distributed as dist
     from qlinear.kernels.w4a16_matmul import w4a16_quantize_cuda
     from qlinear.kernels.w8a16_matmul import w8a16_quantize_cuda
+    from qlinear.p2p import PeerExchange
     from qlinear.quantization.int4 import QuantizedLinearInt4
     from qlinear.quantization.int8 import QuantizedLinearInt8
     from qlinear.sharded import ShardedQuantizedLinear, shard_bounds
@@ -525,18 +532,17 @@ def run_sharded(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    reps = max(5, args.steps)
+    reps = max(3, min(args.steps, 7))
     stream = torch.cuda.Stream(device=dev)
     detail = {}
     tot_bytes = 0.0
     tot_s = 0.0
 
-    def timed(graph):
+    def timed(graph, iters):
+        graph.replay()
+        torch.cuda.synchronize(dev)
         ts = []
         for _ in range(reps):
-            flush.fill_(1)
-            torch.cuda.synchronize(dev)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(stream):
@@ -544,7 +550,7 @@ def run_sharded(args):
                 graph.replay()
                 e1.record(stream)
             torch.cuda.synchronize(dev)
-            ts.append(e0.elapsed_time(e1) * 1e-3)
+            ts.append(e0.elapsed_time(e1) * 1e-3 / iters)
         t = statistics.median(ts)
         if world > 1:
             tt = torch.tensor([t], device=dev, dtype=torch.float64)
@@ -552,49 +558,59 @@ def run_sharded(args):
             t = float(tt.item())
         return t
 
+    def capture(fn, iters):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(iters):
+                fn(i)
+        return g
+
+    exchange = PeerExchange(rank, world, max_m=max(SHARDED_MS))
     for wbits in (4, 8):
         for name, K, N, groups in SHARDED_LAYERS:
             n_g = N // groups
             lo, hi = shard_bounds(n_g, rank, world)
             rows = groups * (hi - lo)
-            w = (torch.randn(rows, K, generator=gen, device=dev) * 0.02).half()
-            if wbits == 4:
-                mod = QuantizedLinearInt4(*w4a16_quantize_cuda(w), None)
-            else:
-                mod = QuantizedLinearInt8(*w8a16_quantize_cuda(w), None)
-            del w
-            sh = ShardedQuantizedLinear(mod, N, rank, world, groups=groups)
+            # the same copy count on every rank (collectives must match): sized by the widest shard
+            shard_bytes = groups * ((n_g + world - 1) // world) * K // (2 if wbits == 4 else 1)
+            copies = max(1, min(32, math.ceil(2 * 128e6 / shard_bytes)))
+            shs = []
+            for _ in range(copies):
+                w = (torch.randn(rows, K, generator=gen, device=dev) * 0.02).half()
+                if wbits == 4:
+                    mod = QuantizedLinearInt4(*w4a16_quantize_cuda(w), None)
+                else:
+                    mod = QuantizedLinearInt8(*w8a16_quantize_cuda(w), None)
+                del w
+                sh = ShardedQuantizedLinear(mod, N, rank, world, groups=groups)
+                if groups == 1:
+                    sh.exchange = exchange     # argmax head: keys over NVLink, one kernel
+                shs.append(sh)
+            iters = copies * max(1, math.ceil(16 / copies))
             for M in SHARDED_MS:
                 x = torch.randn(M, K, generator=gen, device=dev).half()
                 with torch.cuda.stream(stream):
-                    y_loc = sh.local_forward(x)
-                    sh.gather(y_loc)
-                    torch.cuda.synchronize(dev)
-                    g_loc, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-                    g_col = torch.cuda.CUDAGraph() if world > 1 else None   # no exchange on one GPU
-                    g_arg = torch.cuda.CUDAGraph() if groups == 1 else None  # greedy head: argmax only
-                    with torch.cuda.graph(g_loc, stream=stream):
-                        sh.local_forward(x)
-                    if g_col is not None:
-                        with torch.cuda.graph(g_col, stream=stream):
-                            sh.gather(y_loc)
-                    with torch.cuda.graph(g_e2e, stream=stream):
+                    y_loc = shs[0].local_forward(x)
+                    for sh in shs:                       # warm-up: every path once per copy
                         sh(x)
-                    if g_arg is not None:
-                        sh.argmax(x)
-                        torch.cuda.synchronize(dev)
-                        with torch.cuda.graph(g_arg, stream=stream):
+                        if groups == 1:
                             sh.argmax(x)
-                t_loc, t_e2e = timed(g_loc), timed(g_e2e)
-                t_col = timed(g_col) if g_col is not None else 0.0
-                t_arg = timed(g_arg) if g_arg is not None else None
+                    torch.cuda.synchronize(dev)
+                    g_loc = capture(lambda i: shs[i % copies].local_forward(x), iters)
+                    g_e2e = capture(lambda i: shs[i % copies](x), iters)
+                    g_col = capture(lambda i: shs[0].gather(y_loc), iters) if world > 1 else None
+                    g_arg = capture(lambda i: shs[i % copies].argmax(x), iters) if groups == 1 else None
+                t_loc, t_e2e = timed(g_loc, iters), timed(g_e2e, iters)
+                t_col = timed(g_col, iters) if g_col is not None else 0.0
+                t_arg = timed(g_arg, iters) if g_arg is not None else None
                 # graphs holding NCCL calls must be gone before the process group is destroyed
                 torch.cuda.synchronize(dev)
                 del g_loc, g_col, g_e2e, g_arg
                 if rank == 0:
                     print(f"[sharded] w{wbits} {name} M={M}: local {t_loc * 1e6:.1f} us, all-gather "
                           f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us"
-                          + (f", argmax head {t_arg * 1e6:.1f} us" if t_arg is not None else ""),
+                          + (f", argmax head {t_arg * 1e6:.1f} us" if t_arg is not None else "")
+                          + f" ({copies} copies, {iters} iterations per graph)",
                           file=sys.stderr, flush=True)
                 lb = layer_bytes(wbits, K, N)
                 detail[f"w{wbits}_{name}_M{M}"] = {
@@ -605,7 +621,8 @@ def run_sharded(args):
                     detail[f"w{wbits}_{name}_M{M}"]["argmax_us"] = round(t_arg * 1e6, 2)
                 tot_bytes += lb
                 tot_s += t_e2e
-            del sh, mod
+            del shs
+    exchange.close()
     from qlinear import _lib
     dev_err = _lib.device_error()
     if dev_err != 0:
@@ -617,7 +634,8 @@ def run_sharded(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "config4: column-sharded lm_head 1536->151936, lm_head 4096->128256, fused "
                                    "gate+up 4096->28672 (2 groups), W4A16 and W8A16, M in {1,16,64}, NCCL "
-                                   "all-gather of fp16 outputs, L2 flushed per replay",
+                                   "all-gather of fp16 outputs (argmax head: keys over NVLink), weight copies "
+                                   "cycled past L2",
                        "parallelism": f"column shards x{world}"},
             "detail": detail}), flush=True)
     if world > 1:

@@ -208,10 +208,41 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
 int ql_argmax_rows_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t col_offset,
                        uint64_t* keys, void* stream);
 
+/* ---------------------------------------------- sharded argmax over NVLink */
+/* One launch per rank computes the row argmax of its logit shard and
+ * exchanges the per-row keys (as ql_argmax_rows_f16) with the other ranks of
+ * the node by plain stores into their exchange buffers over NVLink, then
+ * waits (bounded) for theirs and writes out[m] = the global argmax column.
+ * Replaces the all-gather of the logits before the reference's greedy
+ * argmax (src/engine/paged_engine.py:146-147); no NCCL call.  All ranks
+ * must make the same sequence of calls with the same M.
+ *
+ * Exchange buffers: each rank allocates one (ql_xchg_alloc, sized by
+ * ql_xchg_buffer_bytes for the world size and the largest M), shares the
+ * 64-byte IPC handle with the others, and opens theirs (ql_xchg_open);
+ * peers[q] is rank q's buffer as seen from this rank (peers[rank] = own).
+ * A peer wait that runs out records QL_DEVICE_ERROR_PEER_WAIT (5) in the
+ * device error word. */
+#define QL_XCHG_MAX_RANKS 8
+size_t ql_xchg_buffer_bytes(int world, int max_m);
+int ql_xchg_alloc(size_t bytes, void** buffer, void* ipc_handle /* 64 bytes out */);
+int ql_xchg_free(void* buffer);
+int ql_xchg_open(const void* ipc_handle /* 64 bytes */, void** peer_buffer);
+int ql_xchg_close(void* peer_buffer);
+int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t col_offset,
+                           int rank, int world, int max_m, void* const* peers, int64_t* out,
+                           void* stream);
+
 /* ------------------------------------------------------------- diagnostics */
 const char* ql_strerror(int status);
 /* Version as (major << 16) | (minor << 8) | patch. */
 int ql_version(void);
+/* Device error codes (ql_device_error). */
+#define QL_DEVICE_ERROR_FULL_WAIT   1   /* a consumer waited too long for a weight stage  */
+#define QL_DEVICE_ERROR_EMPTY_WAIT  2   /* the producer waited too long for a free stage  */
+#define QL_DEVICE_ERROR_MMA_WAIT    3   /* a tensor-core completion wait ran out          */
+#define QL_DEVICE_ERROR_TMEM        4   /* tensor-memory allocation failed                */
+#define QL_DEVICE_ERROR_PEER_WAIT   5   /* another rank's argmax keys never arrived       */
 /* Kernels never trap: a bounded wait that runs out records a code in a
  * device-global word, and the kernel lets its copies in flight land and
  * returns early.  These read (and clear)

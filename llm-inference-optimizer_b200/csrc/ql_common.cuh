@@ -21,6 +21,7 @@ enum DeviceError : unsigned {
   kDevErrEmptyWait = 2,     // producer waited too long for a free stage
   kDevErrMmaWait = 3,       // tensor-core completion wait ran out
   kDevErrTmem = 4,          // TMEM allocation failed
+  kDevErrPeerWait = 5,      // another rank's exchange data never arrived
 };
 
 // Budget of any single bounded wait, in SM clock cycles.  %clock64 is

@@ -20,6 +20,7 @@
 #include "../../include/qlinear.h"
 #include "ql_common.cuh"
 #include "qargmax.cuh"
+#include "qxchg.cuh"
 #include "qformat.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
@@ -809,6 +810,98 @@ int ql_argmax_rows_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t
   return launch(ql::amax::argmax_rows_kernel, dim3((unsigned)cdiv(N, span), (unsigned)M), dim3(256), 0, s, false,
                 static_cast<const __half*>(x), (long long)ldx, (int)N, span, (long long)col_offset, vec,
                 reinterpret_cast<unsigned long long*>(keys));
+}
+
+size_t ql_xchg_buffer_bytes(int world, int max_m) {
+  if (world < 1 || world > QL_XCHG_MAX_RANKS || max_m < 1 || max_m > 65535) return 0;
+  return ql::xchg::layout(world, max_m).total;
+}
+
+int ql_xchg_alloc(size_t bytes, void** buffer, void* ipc_handle) {
+  if (!buffer || !ipc_handle) return QL_ERR_NULL_POINTER;
+  if (bytes == 0) return QL_ERR_BAD_SHAPE;
+  int st;
+  if (!current_device(&st)) return st;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return QL_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *buffer = p;
+  return QL_OK;
+}
+
+int ql_xchg_free(void* buffer) {
+  if (!buffer) return QL_OK;
+  if (cudaFree(buffer) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  return QL_OK;
+}
+
+int ql_xchg_open(const void* ipc_handle, void** peer_buffer) {
+  if (!ipc_handle || !peer_buffer) return QL_ERR_NULL_POINTER;
+  int st;
+  if (!current_device(&st)) return st;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  *peer_buffer = p;
+  return QL_OK;
+}
+
+int ql_xchg_close(void* peer_buffer) {
+  if (!peer_buffer) return QL_OK;
+  if (cudaIpcCloseMemHandle(peer_buffer) != cudaSuccess) {
+    cudaGetLastError();
+    return QL_ERR_CUDA;
+  }
+  return QL_OK;
+}
+
+int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t col_offset, int rank, int world,
+                           int max_m, void* const* peers, int64_t* out, void* stream) {
+  if (!x || !peers || !out) return QL_ERR_NULL_POINTER;
+  if (world < 1 || world > QL_XCHG_MAX_RANKS || rank < 0 || rank >= world) return QL_ERR_BAD_SHAPE;
+  if (M < 1 || M > max_m || max_m > 65535 || N <= 0 || N > INT_MAX || col_offset < 0 ||
+      col_offset + N > 0xFFFFFFFFLL)
+    return QL_ERR_BAD_SHAPE;
+  if (ldx < N) return QL_ERR_BAD_STRIDE;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  ql::xchg::Params p;
+  p.x = static_cast<const __half*>(x);
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.span = 8192;
+  p.vec = aligned16(x) && ldx % 8 == 0 && N % 8 == 0;
+  p.col_offset = col_offset;
+  p.rank = rank;
+  p.world = world;
+  p.max_m = max_m;
+  for (int q = 0; q < ql::xchg::kMaxRanks; ++q) {
+    p.peer[q] = q < world ? static_cast<unsigned char*>(peers[q]) : nullptr;
+    if (q < world && !p.peer[q]) return QL_ERR_NULL_POINTER;
+  }
+  p.out = reinterpret_cast<long long*>(out);
+  p.err = dev->err_word;
+  return launch(ql::xchg::argmax_exchange_kernel, dim3((unsigned)cdiv(N, p.span), (unsigned)M), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), false, p);
 }
 
 // Once per device, with that device current: the host-side name of

@@ -1,0 +1,152 @@
+// qxchg.cuh — sharded-lm_head argmax in one kernel: local reduction plus a
+// push exchange of the per-row keys over NVLink peer memory.
+//
+// Every rank owns an exchange buffer (plain device memory shared with the
+// other ranks of the node through CUDA IPC):
+//   [0, 256)            flags[world]  u32: epoch of the last keys received from rank q
+//   [256, 256 + KB)     keys[2][world][max_m] u64: by epoch parity, by source rank
+//   then                scratch[max_m] u64: this rank's running row maxima
+//   then                state: counter u32 (CTAs arrived), epoch u32 (calls done)
+// Only the owner touches scratch and state; peers write keys and flags.
+//
+// One launch (grid (chunks, M)): each CTA reduces its column chunk of one
+// row to a key (qargmax.cuh) and merges it into scratch with a 64-bit atomic
+// max; the last CTA to arrive stores the M keys into keys[e & 1][rank] of
+// every rank's buffer, fences at system scope, raises flags[rank] = e on
+// every rank, waits (bounded) until all flags[q] in its own buffer reach e,
+// and writes out[m] = the column of max_q keys[e & 1][q][m].  A rank can be
+// at most one call ahead of another (it needs everybody's flag of the call
+// before), so two key banks by epoch parity are enough.  Ranks must make
+// the same sequence of calls.
+#pragma once
+
+#include "qargmax.cuh"
+
+namespace ql {
+namespace xchg {
+
+constexpr int kMaxRanks = 8;
+
+struct Layout {
+  size_t keys, scratch, state, total;
+};
+__host__ __device__ inline Layout layout(int world, int max_m) {
+  Layout l;
+  l.keys = 256;
+  l.scratch = l.keys + (size_t)2 * world * max_m * 8;
+  l.state = l.scratch + (size_t)max_m * 8;
+  l.total = (l.state + 8 + 255) / 256 * 256;
+  return l;
+}
+
+struct Params {
+  const __half* x;
+  long long ldx;
+  int M, N, span, vec;
+  long long col_offset;
+  int rank, world, max_m;
+  unsigned char* peer[kMaxRanks];   // exchange buffer of every rank (peer[rank] = own)
+  long long* out;                   // [M] argmax columns
+  unsigned* err;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  return *reinterpret_cast<const volatile unsigned long long*>(p);
+}
+
+__global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
+  const Layout L = layout(p.world, p.max_m);
+  unsigned char* own = p.peer[p.rank];
+  unsigned long long* scratch = reinterpret_cast<unsigned long long*>(own + L.scratch);
+  unsigned* counter = reinterpret_cast<unsigned*>(own + L.state);
+  unsigned* epoch_done = counter + 1;
+  __shared__ unsigned long long red[8];
+  __shared__ int is_last;
+
+  // ---- local reduction of this CTA's chunk of row m
+  const int m = blockIdx.y;
+  const int c0 = blockIdx.x * p.span;
+  const int c1 = min(p.N, c0 + p.span);
+  const unsigned short* row = reinterpret_cast<const unsigned short*>(p.x + (long long)m * p.ldx);
+  unsigned long long best = 0ull;
+  if (p.vec) {
+    for (int c = c0 + (int)threadIdx.x * 8; c < c1; c += 256 * 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+      const unsigned w[4] = {v.x, v.y, v.z, v.w};
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] & 0xFFFFu), p.col_offset + c + 2 * j));
+        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] >> 16), p.col_offset + c + 2 * j + 1));
+      }
+    }
+  } else {
+    for (int c = c0 + (int)threadIdx.x; c < c1; c += 256) best = amax::umax64(best, amax::row_key(row[c], p.col_offset + c));
+  }
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = amax::umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = red[0];
+    for (int w = 1; w < 8; ++w) b = amax::umax64(b, red[w]);
+    atomicMax(scratch + m, b);
+    __threadfence();
+    const unsigned total = gridDim.x * gridDim.y;
+    is_last = atomicAdd(counter, 1u) == total - 1;
+    if (is_last) __threadfence();
+  }
+  __syncthreads();
+  if (!is_last) return;
+
+  // ---- last CTA: push, signal, wait, combine
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_done) + 1u;
+  const int bank = (int)(e & 1u);
+  for (int q = 0; q < p.world; ++q) {
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(p.peer[q] + L.keys) + ((size_t)bank * p.world + p.rank) * p.max_m;
+    for (int i = threadIdx.x; i < p.M; i += blockDim.x) dst[i] = ld_volatile_u64(scratch + i);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    unsigned* flag = reinterpret_cast<unsigned*>(p.peer[threadIdx.x]) + p.rank;
+    st_release_sys(flag, e);
+  }
+  // wait for every rank's keys of this call (bounded)
+  if (threadIdx.x < p.world) {
+    const unsigned* flag = reinterpret_cast<const unsigned*>(own) + threadIdx.x;
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys(flag) - e) < 0) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        atomicCAS(p.err, 0u, kDevErrPeerWait);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  const unsigned long long* keys =
+      reinterpret_cast<const unsigned long long*>(own + L.keys) + (size_t)bank * p.world * p.max_m;
+  for (int i = threadIdx.x; i < p.M; i += blockDim.x) {
+    unsigned long long b = 0ull;
+    for (int q = 0; q < p.world; ++q) b = amax::umax64(b, ld_volatile_u64(keys + (size_t)q * p.max_m + i));
+    p.out[i] = (long long)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull));
+    scratch[i] = 0ull;                       // ready for the next call
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *counter = 0u;
+    *reinterpret_cast<volatile unsigned*>(epoch_done) = e;
+  }
+}
+
+}  // namespace xchg
+}  // namespace ql

@@ -32,6 +32,13 @@ QL_DTYPE_BF16 = 2
 
 QL_STATIC_WS_BYTES = 2 * 1024 * 1024
 
+QL_DEVICE_ERROR_FULL_WAIT = 1
+QL_DEVICE_ERROR_EMPTY_WAIT = 2
+QL_DEVICE_ERROR_MMA_WAIT = 3
+QL_DEVICE_ERROR_TMEM = 4
+QL_DEVICE_ERROR_PEER_WAIT = 5
+QL_XCHG_MAX_RANKS = 8
+
 QL_W4_LAYOUT_SPLIT_HALF = 0
 QL_W4_LAYOUT_ADJACENT = 1
 
@@ -63,6 +70,13 @@ SIGNATURES = {
     "ql_w8a16_quantize": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "ql_w4a16_quantize": (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp]),
     "ql_argmax_rows_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "ql_xchg_buffer_bytes": (_sz, [_int, _int]),
+    "ql_xchg_alloc": (_int, [_sz, ctypes.POINTER(_vp), _vp]),
+    "ql_xchg_free": (_int, [_vp]),
+    "ql_xchg_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "ql_xchg_close": (_int, [_vp]),
+    "ql_argmax_exchange_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(_vp), _vp,
+                                      _vp]),
     "ql_strerror": (ctypes.c_char_p, [_int]),
     "ql_version": (_int, []),
     "ql_device_error": (_int, [ctypes.POINTER(_int)]),

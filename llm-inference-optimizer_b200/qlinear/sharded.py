@@ -79,6 +79,7 @@ class ShardedQuantizedLinear(nn.Module):
         self.group = group
         self.local_fn = local_fn
         self.key_fn = key_fn
+        self.exchange = None          # optional qlinear.p2p.PeerExchange for argmax
         n = out_features // groups
         self.block = (n + world - 1) // world          # padded per-rank width of one group
         self.widths = [shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0] for r in range(world)]
@@ -155,13 +156,17 @@ class ShardedQuantizedLinear(nn.Module):
 
         Each rank reduces its columns to one key per row (value, global
         column; ties to the smallest column, as torch.argmax), the ranks
-        all-gather the keys (8 bytes per row and rank) and every rank takes
-        the max.  Equals torch.argmax(self(x), dim=-1).  groups == 1 only."""
+        exchange the keys (8 bytes per row and rank) and every rank takes the
+        max: with an attached PeerExchange in one kernel over NVLink, else
+        through an NCCL all-gather.  Equals torch.argmax(self(x), dim=-1).
+        groups == 1 only."""
         assert self.groups == 1, "argmax is defined for a single output block"
         K = self.in_features
         x2 = x.reshape(-1, K)
         y = self.local_fn(self.local, x2)                       # [M, widths[rank]]
         lo = shard_bounds(self.out_features, self.rank, self.world)[0]
+        if self.exchange is not None:                           # one kernel, keys over NVLink
+            return self.exchange.argmax(y, lo).reshape(x.shape[:-1])
         keys = self.key_fn(y, lo)                               # [M] int64 key bits
         if self.world > 1:
             buf = torch.empty(self.world * keys.numel(), dtype=keys.dtype, device=keys.device)

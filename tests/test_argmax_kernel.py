@@ -51,3 +51,63 @@ def test_sharded_module_argmax_single_rank():
     sh = ShardedQuantizedLinear.from_quantized(q, 0, 1)
     x = make_x(5, 1536, seed=4).cuda()
     assert torch.equal(sh.argmax(x), torch.argmax(q(x), dim=-1))
+
+
+def test_exchange_single_rank_matches_torch_and_replays():
+    """World of one: the fused kernel's own push/flag/combine path, eagerly
+    and from a CUDA graph replayed several times (epochs advance)."""
+    from qlinear.p2p import PeerExchange
+    px = PeerExchange(0, 1, max_m=16)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(1)
+        y = torch.randn(16, 30000, generator=g, device="cuda").half()
+        y[:, 123] = y[:, 29000] = 50.0
+        want = torch.argmax(y, dim=-1)
+        assert torch.equal(px.argmax(y, 0), want)
+        assert torch.equal(px.argmax(y[:5], 0), want[:5])
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                out = px.argmax(y, 0)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(5):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+        del graph
+        from qlinear import _lib
+        assert _lib.device_error() == 0
+    finally:
+        px.close()
+
+
+def test_exchange_peer_wait_is_bounded():
+    """A peer that never signals: the kernel gives up after its wait budget
+    (about 2 s), records QL_DEVICE_ERROR_PEER_WAIT and returns; the context
+    stays usable.  The "peer" is a second local buffer nobody writes flags to."""
+    import ctypes
+    from qlinear import _lib
+    lib = _lib.load()
+    nbytes = lib.ql_xchg_buffer_bytes(2, 4)
+    bufs = []
+    for _ in range(2):
+        p, h = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        _lib.check(lib.ql_xchg_alloc(nbytes, ctypes.byref(p), h))
+        bufs.append(p.value)
+    try:
+        _lib.clear_device_error()
+        peers = (ctypes.c_void_p * 2)(*bufs)
+        y = torch.randn(4, 1000, device="cuda").half()
+        out = torch.empty(4, dtype=torch.int64, device="cuda")
+        _lib.check(lib.ql_argmax_exchange_f16(y.data_ptr(), 4, 1000, 1000, 0, 0, 2, 4, peers, out.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert _lib.device_error() == _lib.QL_DEVICE_ERROR_PEER_WAIT
+        _lib.clear_device_error()
+        assert torch.equal(argmax_f16(y), torch.argmax(y, dim=-1))     # context still fine
+    finally:
+        for b in bufs:
+            lib.ql_xchg_free(b)

@@ -66,7 +66,26 @@ def _worker(rank, world, port, case, result_q):
         ok, max_abs, rel, b_abs, b_rel = orc.check_parity(y.float().cpu().numpy(), ref, x.numpy(), deq)
         same = torch.equal(y, yg)
         if groups == 1:   # sharded argmax: keys all-gathered, equals argmax of the gathered logits
-            same = same and torch.equal(sh.argmax(xd), torch.argmax(y, dim=-1))
+            want = torch.argmax(y, dim=-1)
+            same = same and torch.equal(sh.argmax(xd), want)
+            # the same through the NVLink exchange kernel, eager and from a graph
+            from qlinear.p2p import PeerExchange
+            sh.exchange = PeerExchange(rank, world, max_m=64)
+            same = same and torch.equal(sh.argmax(xd), want)
+            with torch.cuda.stream(s):
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2, stream=s):
+                    ig = sh.argmax(xd)
+            torch.cuda.current_stream().wait_stream(s)
+            for _ in range(4):
+                ig.zero_()
+                g2.replay()
+                torch.cuda.synchronize()
+                same = same and torch.equal(ig, want)
+            del g2
+            sh.exchange.close()
+            from qlinear import _lib
+            same = same and _lib.device_error() == 0
         del graph
         dist.barrier()
         dist.destroy_process_group()
