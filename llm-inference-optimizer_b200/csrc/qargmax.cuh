@@ -38,6 +38,7 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsig
 __global__ void __launch_bounds__(256) argmax_rows_kernel(const __half* x, long long ldx, int N, int span,
                                                           long long col_offset, int vec,
                                                           unsigned long long* keys) {
+  griddep_wait();   // the logits come from the kernel before (programmatic dependent launch)
   const int m = blockIdx.y;
   const int c0 = blockIdx.x * span;
   const int c1 = min(N, c0 + span);

@@ -605,16 +605,14 @@ int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
 }
 
 // Where the tensor-core GEMM replaces the decode kernel (measured on B200):
-// from 65 batch rows always, and from 16 on wide layers (lm_head, fused
-// MLP projections), where decoding the weights once for the whole batch
-// beats the decode kernel's two n8 batch tiles per CTA.
-constexpr int64_t kGemmMinM = 65;
+// from 48 batch rows always (the decode kernel re-decodes the weights for
+// every 16-row batch chunk); from 16 on wide layers (lm_head, fused MLP
+// projections); for int8 from 24 rows when K is long.
+constexpr int64_t kGemmMinM = 48;
 constexpr int64_t kGemmMinMWide = 16;
 constexpr int64_t kWideN = 12288;
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
-  (void)wbits;
-  (void)K;
-  return M >= kGemmMinM || (M >= kGemmMinMWide && N >= kWideN);
+  return M >= kGemmMinM || (M >= kGemmMinMWide && N >= kWideN) || (wbits == 8 && M >= 24 && K >= 4096);
 }
 
 int run_linear(const LinearArgs& a) {
@@ -807,7 +805,7 @@ int ql_argmax_rows_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int64_t
   }
   const int vec = aligned16(x) && ldx % 8 == 0 && N % 8 == 0;
   const int span = 8192;   // columns per CTA
-  return launch(ql::amax::argmax_rows_kernel, dim3((unsigned)cdiv(N, span), (unsigned)M), dim3(256), 0, s, false,
+  return launch(ql::amax::argmax_rows_kernel, dim3((unsigned)cdiv(N, span), (unsigned)M), dim3(256), 0, s, true,
                 static_cast<const __half*>(x), (long long)ldx, (int)N, span, (long long)col_offset, vec,
                 reinterpret_cast<unsigned long long*>(keys));
 }
@@ -901,7 +899,7 @@ int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int
   p.out = reinterpret_cast<long long*>(out);
   p.err = dev->err_word;
   return launch(ql::xchg::argmax_exchange_kernel, dim3((unsigned)cdiv(N, p.span), (unsigned)M), dim3(256), 0,
-                static_cast<cudaStream_t>(stream), false, p);
+                static_cast<cudaStream_t>(stream), true, p);
 }
 
 // Once per device, with that device current: the host-side name of

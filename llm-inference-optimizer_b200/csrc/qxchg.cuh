@@ -71,6 +71,10 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
   __shared__ unsigned long long red[8];
   __shared__ int is_last;
 
+  // the logits come from the kernel before (launched with programmatic
+  // dependent launch, this kernel is resident early and waits here)
+  griddep_wait();
+
   // ---- local reduction of this CTA's chunk of row m
   const int m = blockIdx.y;
   const int c0 = blockIdx.x * p.span;

@@ -95,7 +95,7 @@ def test_gemm_prefill_shapes(wbits):
         else:
             q = QuantizedLinearInt8.from_linear(lin)
             y32, deq = _oracle8(x, q)
-        out = q.cuda()(x.cuda())          # default dispatch: M >= 65 takes the tensor-core path
+        out = q.cuda()(x.cuda())          # default dispatch: M >= 48 takes the tensor-core path
         assert_parity(out, y32, x.numpy(), deq, f"prefill w{wbits} K{K} N{N} M{M}")
 
 
