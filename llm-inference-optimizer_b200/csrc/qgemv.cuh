@@ -200,9 +200,10 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, ui
       #pragma unroll
       for (int n = 0; n < NS; ++n) {
         if (LAYOUT == 0) {
+          // permuted decode: the staged activations are in the matching order
           uint32_t al01, al23, ah01, ah23, bl01, bl23, bh01, bh23;
-          dec_w4_split(wA[n][j], al01, al23, ah01, ah23);
-          dec_w4_split(wB[n][j], bl01, bl23, bh01, bh23);
+          dec_w4_split_perm(wA[n][j], al01, al23, ah01, ah23);
+          dec_w4_split_perm(wB[n][j], bl01, bl23, bh01, bh23);
           #pragma unroll
           for (int t = 0; t < MT; ++t) {
             mma_16816(part[n][0][t], al01, bl01, al23, bl23, bx0[n][t][2 * j], bx0[n][t][2 * j + 1]);
@@ -210,8 +211,8 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, ui
           }
         } else {
           uint32_t a01, a23, a45, a67, b01, b23, b45, b67;
-          dec_w4_adjacent(wA[n][j], a01, a23, a45, a67);
-          dec_w4_adjacent(wB[n][j], b01, b23, b45, b67);
+          dec_w4_adjacent_perm(wA[n][j], a01, a23, a45, a67);
+          dec_w4_adjacent_perm(wB[n][j], b01, b23, b45, b67);
           const int jj = (j & 1) * 4;
           #pragma unroll
           for (int t = 0; t < MT; ++t) {
@@ -404,6 +405,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       for (int v = ctid; v < nvec; v += nct) {
         uint4 val = make_uint4(0u, 0u, 0u, 0u);
         if (kx0 + v * 8 < p.K) val = ldg_cg_v4(xrow + v * 8);
+        if (WBITS == 4) val = stage_x_perm<LAYOUT>(val);   // k order of the permuted int4 decode
         *reinterpret_cast<uint4*>(srow + v * 8) = val;
       }
     }

@@ -202,6 +202,48 @@ __device__ __forceinline__ void dec_w4_split(uint32_t u, uint32_t& lo01, uint32_
   hi23 = h2_fma(lop3_and_or(t1, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
 }
 
+// The same nibbles decoded without byte permutes, for activations staged in
+// a permuted k order (stage_x_perm):
+//   split-half: u = bytes b0..b3 (k j..j+3 low, k j+64.. high nibbles) ->
+//     lo02 = (k0, k2), lo13 = (k1, k3), hi02 = (k64, k66), hi13 = (k65, k67)
+//   adjacent:   u = k 0..7 -> p04 = (k0, k4), p15 = (k1, k5), p26, p37
+// Exact: the same integer values as the decoders above, in another order.
+__device__ __forceinline__ void dec_w4_split_perm(uint32_t u, uint32_t& lo02, uint32_t& lo13,
+                                                  uint32_t& hi02, uint32_t& hi13) {
+  const uint32_t v = u >> 8;
+  lo02 = h2_sub(lop3_and_or(u, 0x000F000Fu, kH2Magic), kH2_1032);
+  lo13 = h2_sub(lop3_and_or(v, 0x000F000Fu, kH2Magic), kH2_1032);
+  hi02 = h2_fma(lop3_and_or(u, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+  hi13 = h2_fma(lop3_and_or(v, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+}
+__device__ __forceinline__ void dec_w4_adjacent_perm(uint32_t u, uint32_t& p04, uint32_t& p15,
+                                                     uint32_t& p26, uint32_t& p37) {
+  const uint32_t v = u >> 8;
+  p04 = h2_sub(lop3_and_or(u, 0x000F000Fu, kH2Magic), kH2_1032);
+  p15 = h2_fma(lop3_and_or(u, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+  p26 = h2_sub(lop3_and_or(v, 0x000F000Fu, kH2Magic), kH2_1032);
+  p37 = h2_fma(lop3_and_or(v, 0x00F000F0u, kH2Magic), kH2_1_16, kH2_m72);
+}
+// Activation words (8 halves, k 0..7) in the order the permuted decoders
+// pair them: split-half (k0,k2)(k1,k3)(k4,k6)(k5,k7); adjacent
+// (k0,k4)(k1,k5)(k2,k6)(k3,k7).
+template <int LAYOUT>
+__device__ __forceinline__ uint4 stage_x_perm(uint4 v) {
+  uint4 r;
+  if (LAYOUT == 0) {
+    r.x = __byte_perm(v.x, v.y, 0x5410);
+    r.y = __byte_perm(v.x, v.y, 0x7632);
+    r.z = __byte_perm(v.z, v.w, 0x5410);
+    r.w = __byte_perm(v.z, v.w, 0x7632);
+  } else {
+    r.x = __byte_perm(v.x, v.z, 0x5410);
+    r.y = __byte_perm(v.x, v.z, 0x7632);
+    r.z = __byte_perm(v.y, v.w, 0x5410);
+    r.w = __byte_perm(v.y, v.w, 0x7632);
+  }
+  return r;
+}
+
 // Adjacent-pair int4: byte i holds k = 2i (low nibble) and 2i+1 (high).
 // u = bytes b0..b3 -> k 0..7; outputs p01 = (k0,k1), p23, p45, p67.
 __device__ __forceinline__ void dec_w4_adjacent(uint32_t u, uint32_t& p01, uint32_t& p23,
