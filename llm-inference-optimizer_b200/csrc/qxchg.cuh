@@ -3,21 +3,21 @@
 //
 // Every rank owns an exchange buffer (plain device memory shared with the
 // other ranks of the node through CUDA IPC):
-//   [0, 256)            flags[world]  u32: epoch of the last keys received from rank q
-//   [256, 256 + KB)     keys[2][world][max_m] u64: by epoch parity, by source rank
+//   [0, KB)             keys[2][world][max_m] u64: by epoch parity, by source rank
 //   then                scratch[max_m] u64: this rank's running row maxima
 //   then                state: counter u32 (CTAs arrived), epoch u32 (calls done)
-// Only the owner touches scratch and state; peers write keys and flags.
+// Only the owner touches scratch and state; peers write keys.
 //
 // One launch (grid (chunks, M)): each CTA reduces its column chunk of one
-// row to a key (qargmax.cuh) and merges it into scratch with a 64-bit atomic
-// max; the last CTA to arrive stores the M keys into keys[e & 1][rank] of
-// every rank's buffer, fences at system scope, raises flags[rank] = e on
-// every rank, waits (bounded) until all flags[q] in its own buffer reach e,
-// and writes out[m] = the column of max_q keys[e & 1][q][m].  A rank can be
-// at most one call ahead of another (it needs everybody's flag of the call
-// before), so two key banks by epoch parity are enough.  Ranks must make
-// the same sequence of calls.
+// row to a 48-bit key (qargmax.cuh) and merges it into scratch with a 64-bit
+// atomic max; the last CTA to arrive stores, for every row, the key tagged
+// with the call's epoch in bits 48..63 into keys[e & 1][rank][m] of every
+// rank's buffer — one 8-byte store each, which a reader sees whole, so no
+// fence or separate flag is needed — then polls (bounded) its own buffer
+// until every rank's slot carries the epoch, and writes out[m] = the column
+// of the largest key.  A rank can be at most one call ahead of another (it
+// needs everybody's keys of the call before), so two banks by epoch parity
+// are enough.  Ranks must make the same sequence of calls.
 #pragma once
 
 #include "qargmax.cuh"
@@ -32,7 +32,7 @@ struct Layout {
 };
 __host__ __device__ inline Layout layout(int world, int max_m) {
   Layout l;
-  l.keys = 256;
+  l.keys = 0;
   l.scratch = l.keys + (size_t)2 * world * max_m * 8;
   l.state = l.scratch + (size_t)max_m * 8;
   l.total = (l.state + 8 + 255) / 256 * 256;
@@ -50,17 +50,13 @@ struct Params {
   unsigned* err;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
   return *reinterpret_cast<const volatile unsigned long long*>(p);
 }
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+  *reinterpret_cast<volatile unsigned long long*>(p) = v;
+}
+constexpr unsigned long long kKeyMask = 0xFFFFFFFFFFFFull;   // the 48 key bits
 
 __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
   const Layout L = layout(p.world, p.max_m);
@@ -110,38 +106,33 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
   __syncthreads();
   if (!is_last) return;
 
-  // ---- last CTA: push, signal, wait, combine
+  // ---- last CTA: push tagged keys, wait for every rank's, combine
   const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_done) + 1u;
   const int bank = (int)(e & 1u);
+  const unsigned long long tag = (unsigned long long)((e & 0x7FFFu) | 0x8000u) << 48;   // never 0
   for (int q = 0; q < p.world; ++q) {
     unsigned long long* dst =
         reinterpret_cast<unsigned long long*>(p.peer[q] + L.keys) + ((size_t)bank * p.world + p.rank) * p.max_m;
-    for (int i = threadIdx.x; i < p.M; i += blockDim.x) dst[i] = ld_volatile_u64(scratch + i);
+    for (int i = threadIdx.x; i < p.M; i += blockDim.x) st_volatile_u64(dst + i, tag | ld_volatile_u64(scratch + i));
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < p.world) {
-    unsigned* flag = reinterpret_cast<unsigned*>(p.peer[threadIdx.x]) + p.rank;
-    st_release_sys(flag, e);
-  }
-  // wait for every rank's keys of this call (bounded)
-  if (threadIdx.x < p.world) {
-    const unsigned* flag = reinterpret_cast<const unsigned*>(own) + threadIdx.x;
-    const long long t0 = clock64();
-    while ((int)(ld_acquire_sys(flag) - e) < 0) {
-      if (clock64() - t0 > kWaitBudgetCycles) {
-        atomicCAS(p.err, 0u, kDevErrPeerWait);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  __syncthreads();
-  const unsigned long long* keys =
-      reinterpret_cast<const unsigned long long*>(own + L.keys) + (size_t)bank * p.world * p.max_m;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(own + L.keys) + (size_t)bank * p.world * p.max_m;
   for (int i = threadIdx.x; i < p.M; i += blockDim.x) {
     unsigned long long b = 0ull;
-    for (int q = 0; q < p.world; ++q) b = amax::umax64(b, ld_volatile_u64(keys + (size_t)q * p.max_m + i));
+    for (int q = 0; q < p.world; ++q) {
+      const unsigned long long* slot = keys + (size_t)q * p.max_m + i;
+      unsigned long long v = ld_volatile_u64(slot);
+      if ((v & ~kKeyMask) != tag) {               // bounded wait for rank q's key of this call
+        const long long t0 = clock64();
+        while (((v = ld_volatile_u64(slot)) & ~kKeyMask) != tag) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            atomicCAS(p.err, 0u, kDevErrPeerWait);
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      b = amax::umax64(b, v & kKeyMask);
+    }
     p.out[i] = (long long)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull));
     scratch[i] = 0ull;                       // ready for the next call
   }
