@@ -194,6 +194,38 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
                       int qmin, int layout, uint8_t* w_packed, void* scales,
                       void* stream);
 
+/* ----------------------------------------------------- fused gate+up SwiGLU */
+/* out[M, N] = silu(x @ gate^T) * (x @ up^T) from ONE quantized weight of 2N
+ * stacked rows (rows 0..N-1 = gate_proj, N..2N-1 = up_proj; for int4 the
+ * scales are [K/128, lds >= 2N], for int8 scale[2N]; bias [2N] or NULL).
+ * Replaces the two projections and the activation of the reference's MLP
+ * forward, act_fn(gate_proj(x)) * up_proj(x) (HF Qwen2MLP; the reference
+ * fuses only the elementwise part, src/kernels/fused_swiglu_triton.py:21-53).
+ * The decode kernel applies SwiGLU in its epilogue (fp32, one rounding) and
+ * never stores the [M, 2N] product; where the dispatch picks the tensor-core
+ * kernel, or the decode kernel has no K-unsplit plan, the product goes
+ * through the workspace (size from the *_workspace_size functions; 0 when
+ * the fused path runs) and an elementwise kernel. */
+int ql_w8a16_gate_up_silu(const void* x, int x_dtype,
+                          const void* w_q, const void* scale, int scale_dtype,
+                          const void* bias, int bias_dtype,
+                          void* out,
+                          int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldw, int64_t ldo,
+                          void* workspace, size_t workspace_bytes,
+                          unsigned flags, void* stream);
+int ql_w4a16_gate_up_silu(const void* x, int x_dtype,
+                          const void* w_packed, int layout,
+                          const void* scales,
+                          const void* bias, int bias_dtype,
+                          void* out,
+                          int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldw, int64_t lds, int64_t ldo,
+                          void* workspace, size_t workspace_bytes,
+                          unsigned flags, void* stream);
+size_t ql_w8a16_gate_up_silu_workspace_size(int64_t M, int64_t N, int64_t K);
+size_t ql_w4a16_gate_up_silu_workspace_size(int64_t M, int64_t N, int64_t K);
+
 /* ------------------------------------------------------------------ argmax */
 /* Row-wise argmax of fp16 logits x[M, ldx] (N columns) as packed keys:
  *   keys[m] = max over n of (ord(x[m, n]) << 32) | (0xFFFFFFFF - (col_offset + n))

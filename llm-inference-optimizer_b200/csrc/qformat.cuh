@@ -243,5 +243,25 @@ __global__ void __launch_bounds__(128) quantize_int4_kernel(const __half* w, lon
   }
 }
 
+// out[m, n] = silu(y[m, n]) * y[m, n + nh] for the [M, 2nh] product of a
+// stacked gate+up weight (fp32 math, one rounding); grid-stride.  y lives in
+// the caller's workspace, which must be left zero-filled (split-K scratch
+// shares it), so every element is cleared after it is read.
+__global__ void __launch_bounds__(256) swiglu_kernel(__half* y, long long ldy, int M, int nh, __half* out,
+                                                     long long ldo) {
+  const long long total = (long long)M * nh;
+  const __half zero = __float2half(0.f);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / nh), n = (int)(i - (long long)m * nh);
+    __half* gp = y + (long long)m * ldy + n;
+    const float g = __half2float(*gp);
+    const float u = __half2float(gp[nh]);
+    *gp = zero;
+    gp[nh] = zero;
+    out[(long long)m * ldo + n] = __float2half_rn(g / (1.f + __expf(-g)) * u);
+  }
+}
+
 }  // namespace fmt
 }  // namespace ql

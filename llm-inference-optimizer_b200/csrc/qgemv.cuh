@@ -78,6 +78,9 @@ struct Params {
   int scale_f32;          // int8 scale dtype
   int bias_f32;           // bias dtype
   int early_weights;      // stream weights before griddepcontrol.wait
+  int swiglu_n;           // > 0: rows [0, n) are gate and [n, 2n) up rows of one stacked
+                          // weight; a block pairs tpc/2 gate tiles with the matching up
+                          // tiles and stores silu(gate) * up, [M, n] (ks == 1 only)
   uint32_t* counters;     // [gridDim.z * nblk] (ks > 1)
   float* partials;        // [gridDim.z][nblk][ks][mc][tpc*16] (ks > 1)
   unsigned* err;          // device error word
@@ -312,6 +315,13 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   // slot's phase q/P.
   const int P = stages / tpc;
   const int nit = (p.nblk - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // blocks of this CTA
+  // first weight row of tile position tt of block blk
+  const int half_tiles = tpc >> 1;
+  auto tile_row = [&](int blk, int t) -> int {
+    if (p.swiglu_n == 0) return blk * rows_cta + t * kTileRows;
+    return t < half_tiles ? (blk * half_tiles + t) * kTileRows
+                          : p.swiglu_n + (blk * half_tiles + t - half_tiles) * kTileRows;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -343,7 +353,7 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
           *abort = 1;
           break;
         }
-        const int row = ((int)blockIdx.x + it * (int)gridDim.x) * rows_cta + tt * kTileRows;
+        const int row = tile_row((int)blockIdx.x + it * (int)gridDim.x, tt);
         const int kbg = kb0 + kc * kb_stage;               // first k-block of the stage
         uint8_t* dst = ring + (size_t)s * stage_bytes;
         mbar_arrive_expect_tx(full + s, stage_tx);
@@ -378,11 +388,10 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     const int G = p.K / 128;
     const int g0 = kb0 * 2;
     const int ng = min(kbc * 2, G - g0);
-    const int row0 = blk * rows_cta;
     const __half* sc = static_cast<const __half*>(p.scale);
     for (int idx = ctid; idx < (ng << rows_log2); idx += nct) {
       const int gl = idx >> rows_log2, r = idx & (rows_cta - 1);
-      const int n = row0 + r;
+      const int n = tile_row(blk, r >> 4) + (r & 15);
       ssc[idx] = n < p.N ? __half2float(sc[(long long)(g0 + gl) * p.lds + n]) : 0.f;
     }
   };
@@ -499,7 +508,29 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       }
     }
 
-    if (p.ks == 1) {
+    if (p.swiglu_n > 0) {
+      // gate tile t and up tile t + tpc/2 live in different warps: the CTA
+      // meets, then every (row, column) pair is finished and stored once,
+      // silu and product in fp32, one rounding to fp16
+      named_bar_sync(1, nct);
+      const int hrows = half_tiles * kTileRows;
+      for (int idx = ctid; idx < mvalid * hrows; idx += nct) {
+        const int m = idx / hrows, r = idx - m * hrows;
+        const int t = r >> 4, rr = r & 15;
+        float gv = 0.f, uv = 0.f;
+        for (int w2 = 0; w2 < wpt; ++w2) {
+          gv += red[((t * wpt + w2) * MC + m) * kTileRows + rr];
+          uv += red[(((t + half_tiles) * wpt + w2) * MC + m) * kTileRows + rr];
+        }
+        const int n = blk * hrows + r;                       // output column = gate row
+        if (n < p.swiglu_n) {
+          gv = finish_value<WBITS>(p, gv, n);
+          uv = finish_value<WBITS>(p, uv, p.swiglu_n + n);
+          p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
+        }
+      }
+      named_bar_sync(1, nct);   // red (and the block scales) are reused next block
+    } else if (p.ks == 1) {
       // Only the warps of one tile meet here (named barrier 2 + tt), so
       // tiles finish their blocks independently.
       if (wpt > 1) named_bar_sync(2 + tt, wpt * 32); else __syncwarp();

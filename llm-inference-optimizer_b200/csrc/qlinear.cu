@@ -246,13 +246,15 @@ void plan_override(int* tpc, int* ks) {
 constexpr size_t kSmemShared = 110 * 1024;   // two CTAs per SM fit under this
 
 bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, int scale_tma,
-               GemvPlan* out) {
+               GemvPlan* out, int64_t pair_n = 0) {
   const int mt = M <= 8 ? 1 : 2;
   const int mc = 8 * mt;
   const int64_t kbytes = wbits == 4 ? K / 2 : K;
   const int nkb = (int)cdiv(kbytes, 128);
   const int epk = wbits == 4 ? 256 : 128;
-  const int64_t NT = cdiv(N, 16);
+  // pair_n > 0 (fused gate+up): N = 2 * pair_n stacked rows, blocks pair
+  // gate tiles with up tiles, no K-split
+  const int64_t NT = pair_n > 0 ? 2 * cdiv(pair_n, 16) : cdiv(N, 16);
   const int x_rows = (int)std::min<int64_t>(mc, M);
   const int mchunks = (int)cdiv(M, mc);
   if (mchunks > 65535) return false;
@@ -274,7 +276,8 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   for (int tpc : {1, 2, 4, 8}) {
     if (o_tpc > 0 && tpc != o_tpc) continue;
     if (o_tpc <= 0 && tpc > 1 && (int64_t)(tpc / 2) * 16 >= N) continue;
-    const int64_t nblk = cdiv(NT, tpc);
+    if (pair_n > 0 && tpc < 2) continue;
+    const int64_t nblk = pair_n > 0 ? cdiv(cdiv(pair_n, 16), tpc / 2) : cdiv(NT, tpc);
     if (nblk > INT_MAX / 2) continue;
     int last_kbps = -1;
     for (int ks = 1; ks <= nkb; ++ks) {
@@ -283,6 +286,7 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       last_kbps = kbps;
       const int ks_eff = (int)cdiv(nkb, kbps);
       if (o_ks > 0 && ks_eff != o_ks) continue;
+      if (pair_n > 0 && ks_eff != 1) continue;
       if (ks_eff > 65535) continue;
       GemvPlan p;
       p.tpc = tpc;
@@ -399,6 +403,7 @@ struct LinearArgs {
   size_t ws_bytes;
   unsigned flags;
   cudaStream_t stream;
+  int64_t swiglu_n = 0;   // > 0: fused gate+up, N = 2 * swiglu_n stacked weight rows
 };
 
 int run_generic(const LinearArgs& a) {
@@ -426,6 +431,9 @@ int run_generic(const LinearArgs& a) {
 
 int run_generic(const LinearArgs& a);
 
+// A fused gate+up call the decode kernel has no plan for.
+constexpr int kNoPlan = 1;
+
 int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   GemvPlan pl;
   const size_t avail = a.ws ? a.ws_bytes : 0;
@@ -434,7 +442,8 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   const int scale_tma = (a.wbits == 4 && aligned16(a.scale) && a.lds % 8 == 0) ? 1 : 0;
   // no decode plan fits (e.g. a tall K with many batch rows and no
   // workspace for split-K): the portable kernel takes it
-  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, scale_tma, &pl)) return run_generic(a);
+  if (!plan_gemv(a.wbits, a.M, a.N, a.K, dev->sms, avail, scale_tma, &pl, a.swiglu_n))
+    return a.swiglu_n > 0 ? kNoPlan : run_generic(a);
   if (pl.stages < pl.tpc || pl.stages % pl.tpc != 0 || pl.gx < 1 || pl.gx > pl.nblk)
     return QL_ERR_UNSUPPORTED;
   CUtensorMap tm, tms;
@@ -474,6 +483,7 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
   const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
   p.early_weights = pdl ? 1 : 0;
+  p.swiglu_n = (int)a.swiglu_n;
   p.err = dev->err_word;
   if (pl.ks > 1) {
     const size_t counters = ((size_t)pl.nblk * pl.mchunks * 4 + 255) / 256 * 256;
@@ -615,6 +625,42 @@ bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
   return M >= kGemmMinM || (M >= kGemmMinMWide && N >= kWideN) || (wbits == 8 && M >= 24 && K >= 4096);
 }
 
+// Argument checks shared by the linear entry points; out_cols = the
+// columns of `out` (N, or N/2 for the fused gate+up).  QL_OK + *empty when
+// there is nothing to do.
+int check_args(const LinearArgs& a, int64_t out_cols, bool* empty) {
+  *empty = false;
+  if (!a.x || !a.w || !a.scale || !a.out) {
+    if (a.M == 0 || a.N == 0) {
+      *empty = true;
+      return QL_OK;
+    }
+    return QL_ERR_NULL_POINTER;
+  }
+  if (a.M < 0 || a.N < 0 || a.K < 0) return QL_ERR_BAD_SHAPE;
+  if (a.M > INT_MAX || a.N > INT_MAX || a.K > INT_MAX) return QL_ERR_BAD_SHAPE;
+  if (a.wbits == 4 && a.K % 128 != 0) return QL_ERR_BAD_SHAPE;
+  if (a.M == 0 || a.N == 0) {
+    *empty = true;
+    return QL_OK;
+  }
+  const int64_t wrow = a.wbits == 4 ? a.K / 2 : a.K;
+  if (a.ldx < a.K || a.ldw < wrow || a.ldo < out_cols) return QL_ERR_BAD_STRIDE;
+  if (a.wbits == 4 && a.lds < a.N) return QL_ERR_BAD_STRIDE;
+  if (a.scale_dtype != QL_DTYPE_F32 && a.scale_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (a.wbits == 4 && a.scale_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (a.bias && a.bias_dtype != QL_DTYPE_F16 && a.bias_dtype != QL_DTYPE_F32) return QL_ERR_UNSUPPORTED;
+  if (a.wbits == 4 && a.layout != QL_W4_LAYOUT_SPLIT_HALF && a.layout != QL_W4_LAYOUT_ADJACENT)
+    return QL_ERR_UNSUPPORTED;
+  return QL_OK;
+}
+
+bool fast_path_ok(const LinearArgs& a) {
+  const int64_t wrow = a.wbits == 4 ? a.K / 2 : a.K;
+  return a.K > 0 && aligned16(a.x) && a.ldx % 8 == 0 && a.K % 8 == 0 && aligned16(a.w) && a.ldw % 16 == 0 &&
+         wrow % 16 == 0;
+}
+
 int run_linear(const LinearArgs& a) {
   if (!a.x || !a.w || !a.scale || !a.out) {
     if (a.M == 0 || a.N == 0) return QL_OK;
@@ -646,6 +692,50 @@ int run_linear(const LinearArgs& a) {
   return run_gemv(a, dev);
 }
 
+// Fused gate+up with SwiGLU: weights are 2n stacked rows (gate, then up),
+// out[M, n] = silu(x @ gate^T) * (x @ up^T).  The decode kernel does it in
+// its epilogue when the dispatch picks it and it has a K-unsplit plan;
+// otherwise the [M, 2n] product goes through the workspace and an
+// elementwise kernel applies SwiGLU.
+size_t swiglu_temp_bytes(int64_t M, int64_t n) { return ((size_t)M * 2 * n * 2 + 255) / 256 * 256; }
+
+bool swiglu_fused_plan(int wbits, int64_t M, int64_t n, int64_t K, int sms) {
+  if (use_gemm(wbits, M, 2 * n, K)) return false;
+  GemvPlan pl;
+  return plan_gemv(wbits, M, 2 * n, K, sms, 0, 0, &pl, n) && plan_gemv(wbits, M, 2 * n, K, sms, 0, 1, &pl, n);
+}
+
+int run_swiglu(const LinearArgs& a) {
+  const int64_t n = a.swiglu_n;
+  if (n <= 0 || a.N != 2 * n) return QL_ERR_BAD_SHAPE;
+  bool empty;
+  int st = check_args(a, n, &empty);
+  if (st != QL_OK || empty) return st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  const bool fast_ok = fast_path_ok(a);
+  if (fast_ok && !(a.flags & (QL_FLAG_FORCE_GEMM | QL_FLAG_FORCE_GENERIC)) &&
+      ((a.flags & QL_FLAG_FORCE_GEMV) || !use_gemm(a.wbits, a.M, a.N, a.K))) {
+    st = run_gemv(a, dev);
+    if (st != kNoPlan) return st;
+  }
+  const size_t temp = swiglu_temp_bytes(a.M, n);
+  if (!a.ws || a.ws_bytes < temp) return QL_ERR_WORKSPACE;
+  LinearArgs b = a;
+  b.swiglu_n = 0;
+  b.out = a.ws;
+  b.ldo = 2 * n;
+  b.ws = a.ws_bytes > temp ? static_cast<uint8_t*>(a.ws) + temp : nullptr;
+  b.ws_bytes = a.ws_bytes - temp;
+  st = run_linear(b);
+  if (st != QL_OK) return st;
+  const long long total = a.M * n;
+  const unsigned blocks = (unsigned)std::min<int64_t>(cdiv(total, 256), 65535LL * 8);
+  return launch(ql::fmt::swiglu_kernel, dim3(blocks), dim3(256), 0, a.stream, false,
+                static_cast<__half*>(a.ws), (long long)(2 * n), (int)a.M, (int)n,
+                static_cast<__half*>(a.out), (long long)a.ldo);
+}
+
 }  // namespace
 
 // ======================================================================
@@ -671,6 +761,37 @@ int ql_w4a16_linear(const void* x, int x_dtype, const void* w_packed, int layout
   return run_linear(a);
 }
 
+int ql_w8a16_gate_up_silu(const void* x, int x_dtype, const void* w_q, const void* scale, int scale_dtype,
+                          const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldw, int64_t ldo, void* workspace, size_t workspace_bytes,
+                          unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (N <= 0 || N > INT_MAX / 2) return N == 0 ? QL_OK : QL_ERR_BAD_SHAPE;
+  LinearArgs a{8, x, w_q, 0, scale, scale_dtype, bias, bias_dtype, out, M, 2 * N, K, ldx, ldw, 2 * N,
+               ldo, workspace, workspace_bytes, flags, static_cast<cudaStream_t>(stream), N};
+  return run_swiglu(a);
+}
+
+int ql_w4a16_gate_up_silu(const void* x, int x_dtype, const void* w_packed, int layout, const void* scales,
+                          const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldw, int64_t lds, int64_t ldo, void* workspace,
+                          size_t workspace_bytes, unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  if (N <= 0 || N > INT_MAX / 2) return N == 0 ? QL_OK : QL_ERR_BAD_SHAPE;
+  LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, out, M, 2 * N, K, ldx, ldw, lds,
+               ldo, workspace, workspace_bytes, flags, static_cast<cudaStream_t>(stream), N};
+  return run_swiglu(a);
+}
+
+static size_t swiglu_workspace_size(int wbits, int64_t M, int64_t N, int64_t K);
+
+size_t ql_w8a16_gate_up_silu_workspace_size(int64_t M, int64_t N, int64_t K) {
+  return swiglu_workspace_size(8, M, N, K);
+}
+size_t ql_w4a16_gate_up_silu_workspace_size(int64_t M, int64_t N, int64_t K) {
+  return swiglu_workspace_size(4, M, N, K);
+}
+
 static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0 || (wbits == 4 && K % 128 != 0)) return 0;
   int st;
@@ -689,6 +810,15 @@ static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
 }
 
 size_t ql_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(8, M, N, K); }
+
+static size_t swiglu_workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || (wbits == 4 && K % 128 != 0)) return 0;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return 0;
+  if (swiglu_fused_plan(wbits, M, N, K, dev->sms)) return 0;
+  return swiglu_temp_bytes(M, N) + workspace_size(wbits, M, 2 * N, K);
+}
 
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes, int64_t* fields,
                  int nfields) {

@@ -61,6 +61,12 @@ SIGNATURES = {
                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
     "ql_w4a16_linear_static_ws": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _uint, _vp]),
+    "ql_w8a16_gate_up_silu": (_int, [_vp, _int, _vp, _vp, _int, _vp, _int, _vp,
+                                     _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
+    "ql_w4a16_gate_up_silu": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp,
+                                     _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _uint, _vp]),
+    "ql_w8a16_gate_up_silu_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "ql_w4a16_gate_up_silu_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_w8a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_w4a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_gemv_plan": (_int, [_int, _i64, _i64, _i64, _sz, ctypes.POINTER(_i64), _int]),

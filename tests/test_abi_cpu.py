@@ -193,3 +193,20 @@ def test_quantize_model_replaces_every_layer_linear():
     assert "model.layers.0.self_attn.q_proj.weight_packed" in sd
     assert "model.layers.0.self_attn.q_proj.scales" in sd
     assert "model.layers.0.self_attn.q_proj.bias" in sd
+
+
+def test_stacked_gate_up_dequantizes_to_the_stacked_weights():
+    """stack_gate_up concatenates quantized buffers; row-local quantization
+    makes that equal to quantizing the stacked fp16 weight."""
+    from qlinear.kernels.fused_mlp import stack_gate_up
+    from helpers import make_linear
+    g, u = make_linear(256, 40, bias=True, seed=1), make_linear(256, 40, bias=False, seed=2)
+    for cls in (QuantizedLinearInt4, QuantizedLinearInt8):
+        s = stack_gate_up(cls.from_linear(g), cls.from_linear(u))
+        both = torch.nn.Linear(256, 80, bias=True).half()
+        with torch.no_grad():
+            both.weight.copy_(torch.cat([g.weight, u.weight]))
+            both.bias.copy_(torch.cat([g.bias, torch.zeros(40, dtype=torch.float16)]))
+        ref = cls.from_linear(both)
+        assert torch.equal(s.dequantized_weight(), ref.dequantized_weight())
+        assert torch.equal(s.bias, ref.bias)
