@@ -60,24 +60,8 @@ def gate_up_silu(x: torch.Tensor, stacked: nn.Module) -> torch.Tensor:
 def stack_gate_up(gate: nn.Module, up: nn.Module) -> nn.Module:
     """One quantized module with gate's rows then up's rows (quantization is
     row-local, so this equals quantizing the stacked fp16 weight)."""
-    if isinstance(gate, QuantizedLinearInt4) and isinstance(up, QuantizedLinearInt4):
-        assert gate.layout == up.layout
-        bias = None
-        if gate.bias is not None or up.bias is not None:
-            zg = torch.zeros(gate.out_features, dtype=torch.float16, device=gate.scales.device)
-            zu = torch.zeros(up.out_features, dtype=torch.float16, device=up.scales.device)
-            bias = torch.cat([gate.bias if gate.bias is not None else zg, up.bias if up.bias is not None else zu])
-        return QuantizedLinearInt4(torch.cat([gate.weight_packed, up.weight_packed]).contiguous(),
-                                   torch.cat([gate.scales, up.scales], dim=1).contiguous(), bias, layout=gate.layout)
-    if isinstance(gate, QuantizedLinearInt8) and isinstance(up, QuantizedLinearInt8):
-        bias = None
-        if gate.bias is not None or up.bias is not None:
-            zg = torch.zeros(gate.out_features, dtype=torch.float16, device=gate.scale.device)
-            zu = torch.zeros(up.out_features, dtype=torch.float16, device=up.scale.device)
-            bias = torch.cat([gate.bias if gate.bias is not None else zg, up.bias if up.bias is not None else zu])
-        return QuantizedLinearInt8(torch.cat([gate.weight_q, up.weight_q]).contiguous(),
-                                   torch.cat([gate.scale, up.scale]).contiguous(), bias)
-    raise TypeError("gate and up must be quantized with the same format")
+    from .fused_qkv import stack_rows
+    return stack_rows([gate, up])
 
 
 class QuantizedGateUpSiLU(nn.Module):

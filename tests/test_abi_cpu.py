@@ -210,3 +210,18 @@ def test_stacked_gate_up_dequantizes_to_the_stacked_weights():
         ref = cls.from_linear(both)
         assert torch.equal(s.dequantized_weight(), ref.dequantized_weight())
         assert torch.equal(s.bias, ref.bias)
+
+
+def test_stacked_qkv_rows_dequantize_to_the_stacked_weights():
+    from qlinear.kernels.fused_qkv import stack_rows
+    from helpers import make_linear
+    lins = [make_linear(256, n, bias=True, seed=n) for n in (64, 16, 16)]
+    for cls in (QuantizedLinearInt4, QuantizedLinearInt8):
+        s = stack_rows([cls.from_linear(l) for l in lins])
+        both = torch.nn.Linear(256, 96, bias=True).half()
+        with torch.no_grad():
+            both.weight.copy_(torch.cat([l.weight for l in lins]))
+            both.bias.copy_(torch.cat([l.bias for l in lins]))
+        ref = cls.from_linear(both)
+        assert torch.equal(s.dequantized_weight(), ref.dequantized_weight())
+        assert torch.equal(s.bias, ref.bias)

@@ -98,3 +98,45 @@ def test_fused_mlp_in_model(wbits):
     assert out.shape == (1, 14)
     from qlinear import _lib
     assert _lib.device_error() == 0
+
+
+def test_qkv_stacked_matches_oracle():
+    """q/k/v from one stacked launch, each within the north-star bound of its projection."""
+    from qlinear.kernels.fused_qkv import QuantizedQKV
+    from helpers import assert_parity
+    mods = [QuantizedLinearInt4.from_linear(make_linear(1536, n, bias=True, std=0.02, seed=n)) for n in (1536, 256, 256)]
+    qkv = QuantizedQKV.from_quantized(*[m.cuda() for m in mods])
+    x = make_x(3, 1536, seed=9)
+    outs = qkv(x.cuda())
+    for m, o in zip(mods, outs):
+        deq = _deq(m)
+        y = orc.linear_f32(x.numpy(), deq, m.bias.cpu().numpy())
+        assert_parity(o, y, x.numpy(), deq, f"qkv part {m.out_features}")
+
+
+@pytest.mark.parametrize("wbits", [8, 4])
+def test_fused_qkv_and_mlp_in_model(wbits):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    from qlinear.kernels.fused_qkv import fuse_attention_qkv
+    cfg = Qwen2Config(vocab_size=4096, hidden_size=1536, intermediate_size=8960, num_hidden_layers=2,
+                      num_attention_heads=12, num_key_value_heads=2, max_position_embeddings=256,
+                      tie_word_embeddings=False)
+    torch.manual_seed(1)
+    model = Qwen2ForCausalLM(cfg)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(0.0, 0.02)
+    model = model.half().cuda().eval()
+    (quantize_model_int8 if wbits == 8 else quantize_model_int4)(model)
+    ids = torch.randint(0, 4096, (1, 32), generator=torch.Generator().manual_seed(3)).cuda()
+    with torch.no_grad():
+        ref = model(ids).logits.float()
+        ref_gen = model.generate(ids[:, :8], max_new_tokens=6, do_sample=False)
+        assert fuse_attention_qkv(model) == 2
+        assert fuse_mlp_gate_up(model) == 2
+        ours = model(ids).logits.float()
+        gen = model.generate(ids[:, :8], max_new_tokens=6, do_sample=False)
+    cos = torch.nn.functional.cosine_similarity(ours.flatten(), ref.flatten(), dim=0).item()
+    assert cos > 0.9999, cos
+    assert (ours.argmax(-1) == ref.argmax(-1)).float().mean().item() >= 0.98
+    assert gen.shape == ref_gen.shape
