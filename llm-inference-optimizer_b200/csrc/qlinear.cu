@@ -517,7 +517,11 @@ struct GemmPlan {
 
 GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail) {
   GemmPlan g;
-  g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : (M <= 128 || wbits == 8) ? 128 : 256;
+  // int8 stages carry twice the weight bytes, so its widest tile is 192
+  // rows (three 64 KB stages) where int4 takes 256 (three 72 KB stages);
+  // measured: the 192-row int8 tile pays off from M = 1024 (at 512 its 1.4
+  // waves lose to the 128-row tile's 1.9)
+  g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : wbits == 4 ? 256 : M >= 1024 ? 192 : 128;
   g.tiles = cdiv(N, ql::gemm::kTileN) * cdiv(M, g.bn);
   const int64_t nk = K / 128;
   int64_t ks = 1;
@@ -603,7 +607,8 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
     case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.ks);
     case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.ks);
     case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.ks);
-    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 128>(a, tx, tw, p, g.ks);
+    case 192: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.ks);
+    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.ks);
   }
 }
 
