@@ -7,8 +7,8 @@ on): W4A16 group-128 GEMV / skinny GEMM, x fp16 [M, K] ~ N(0,1) with M in
 by the reference's RTN quantizer into the reference's packed format.
 
 One step = every (M, shape) pair over COPIES distinct weight copies per shape
-(24 x 2 x 7.1 MB = 341 MB, 2.7x the 126 MB L2, cycled so no launch finds its
-weights in L2), i.e. 144 kernel launches, recorded once into a CUDA graph.
+(36 x 2 x 7.1 MB = 511 MB, 4.1x the 126 MB L2, cycled so no launch finds its
+weights in L2), i.e. 216 kernel launches, recorded once into a CUDA graph.
 
   value   = algorithmic bytes of all ranks / device time of K steps (GB/s);
             algorithmic bytes per launch = N*K/2 + 2*N*K/128 + 2*M*K + 2*M*N.
@@ -44,10 +44,10 @@ for _p in (str(ROOT), str(ROOT / "llm-inference-optimizer_b200")):
 METRIC = "W4A16/W8A16 decode GEMV HBM GB/s (% of 8 TB/s); prefill GEMM TFLOPS"
 MS = (1, 8, 32)
 SHAPES = ((1536, 8960), (8960, 1536))      # (K, N)
-COPIES = 24
+COPIES = 36
 WORKLOAD = ("config1: W4A16 group-128 GEMV, M in {1,8,32}, (K,N) in {(1536,8960),(8960,1536)}, "
             "reference split-half int4 format, fp16 scales [K/128,N], no bias, "
-            f"{COPIES} weight copies per shape cycled (341 MB > L2)")
+            f"{COPIES} weight copies per shape cycled (511 MB, 4.1x L2)")
 
 
 def algo_bytes(M: int, K: int, N: int) -> int:
@@ -392,7 +392,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms_val / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "global_batch": list(MS), "l2": "inputs larger than L2 "
-                       "(weights cycled; each launch's weights last touched 47 launches earlier)",
+                       "(weights cycled; each launch's weights last touched 71 launches earlier)",
                        "launches_per_step": launches_per_step, "bytes_per_step": nbytes,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
