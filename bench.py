@@ -503,8 +503,10 @@ def run_sharded(args):
     """`--workload sharded`: BASELINE config 4.  Every rank holds its column
     shard of each layer (quantized on the device), runs the local kernel and
     one NCCL all-gather of the fp16 outputs; for the lm_heads the greedy
-    head (argmax only) also runs as one kernel per rank that exchanges the
-    per-row argmax keys over NVLink (qlinear.p2p).  Per (wbits, layer, M),
+    head (argmax only) also runs with the per-row argmax keys exchanged over
+    NVLink (qlinear.p2p) — up to 8 rows as ONE launch per rank (the decode
+    kernel's epilogue makes the keys and runs the exchange), and, for
+    comparison, as the linear followed by the exchange kernel.  Per (wbits, layer, M),
     CUDA graphs of R back-to-back iterations are timed — local compute only,
     the all-gather only, the whole sharded forward, the argmax head — each
     iteration on the next of C distinct weight copies (C x shard bytes >
@@ -600,16 +602,20 @@ def run_sharded(args):
                     g_e2e = capture(lambda i: shs[i % copies](x), iters)
                     g_col = capture(lambda i: shs[0].gather(y_loc), iters) if world > 1 else None
                     g_arg = capture(lambda i: shs[i % copies].argmax(x), iters) if groups == 1 else None
+                    g_arg2 = (capture(lambda i: shs[i % copies].argmax(x, fused=False), iters)
+                              if groups == 1 else None)
                 t_loc, t_e2e = timed(g_loc, iters), timed(g_e2e, iters)
                 t_col = timed(g_col, iters) if g_col is not None else 0.0
                 t_arg = timed(g_arg, iters) if g_arg is not None else None
+                t_arg2 = timed(g_arg2, iters) if g_arg2 is not None else None
                 # graphs holding NCCL calls must be gone before the process group is destroyed
                 torch.cuda.synchronize(dev)
-                del g_loc, g_col, g_e2e, g_arg
+                del g_loc, g_col, g_e2e, g_arg, g_arg2
                 if rank == 0:
                     print(f"[sharded] w{wbits} {name} M={M}: local {t_loc * 1e6:.1f} us, all-gather "
                           f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us"
-                          + (f", argmax head {t_arg * 1e6:.1f} us" if t_arg is not None else "")
+                          + (f", argmax head {t_arg * 1e6:.1f} us (two launches {t_arg2 * 1e6:.1f} us)"
+                             if t_arg is not None else "")
                           + f" ({copies} copies, {iters} iterations per graph)",
                           file=sys.stderr, flush=True)
                 lb = layer_bytes(wbits, K, N)
@@ -619,6 +625,7 @@ def run_sharded(args):
                     "GBps_compute_per_gpu": round(lb / world / t_loc / 1e9, 1)}
                 if t_arg is not None:
                     detail[f"w{wbits}_{name}_M{M}"]["argmax_us"] = round(t_arg * 1e6, 2)
+                    detail[f"w{wbits}_{name}_M{M}"]["argmax_two_launch_us"] = round(t_arg2 * 1e6, 2)
                 tot_bytes += lb
                 tot_s += t_e2e
             del shs
@@ -641,6 +648,157 @@ def run_sharded(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+DECODE_LAYERS = 28
+DECODE_MS = (1, 4, 16, 64)
+# Qwen2.5-1.5B projections per layer: (name, K, N, bias)
+DECODE_LINEARS = (("q", 1536, 1536, True), ("k", 1536, 256, True), ("v", 1536, 256, True),
+                  ("o", 1536, 1536, False), ("gate", 1536, 8960, False), ("up", 1536, 8960, False),
+                  ("down", 8960, 1536, False))
+
+
+def linear_weight_bytes(wbits, K, N, bias):
+    """Stored bytes of one quantized projection: int4 packed + fp16 group
+    scales, or int8 + fp32 row scales; fp16 bias."""
+    w = N * K // 2 + 2 * N * (K // 128) if wbits == 4 else N * K + 4 * N
+    return w + (2 * N if bias else 0)
+
+
+def decode_step_bytes(wbits, M, fused):
+    """Algorithmic bytes of one decode step over all layers: every weight
+    byte once plus each launch's fp16 activations in and out."""
+    per = 0
+    for _, K, N, b in DECODE_LINEARS:
+        per += linear_weight_bytes(wbits, K, N, b)
+    if fused:
+        launches = ((1536, 1536 + 2 * 256), (1536, 1536), (1536, 8960), (8960, 1536))   # qkv, o, gate_up_silu, down
+    else:
+        launches = tuple((K, N) for _, K, N, _ in DECODE_LINEARS)
+    per += sum(2 * M * (K + N) for K, N in launches)
+    return DECODE_LAYERS * per
+
+
+def run_decode_step(args):
+    """`--workload decode_step`: BASELINE config 2.  The seven projections of
+    all 28 layers of a random-init Qwen2.5-1.5B (q/k/v with bias), quantized
+    on the device, run through the public modules for one decode step at M
+    in {1, 4, 16, 64}, W4 and W8 — once as seven launches per layer (the
+    reference's module structure) and once with the fused kernels (q/k/v
+    stacked in one launch, gate+up with the SwiGLU epilogue: four launches
+    per layer).  Each step is one CUDA graph; the step's weights (676 MB W4,
+    1.31 GB W8) exceed L2 several times over, so no flush is needed.
+    Projections feed each other where the model does (o reads q's output,
+    down reads gate's or the fused MLP's output); attention and norms are
+    not part of the path and are left out."""
+    import torch
+    from qlinear.kernels.fused_mlp import QuantizedGateUpSiLU
+    from qlinear.kernels.fused_qkv import QuantizedQKV
+    from qlinear.kernels.w4a16_matmul import w4a16_quantize_cuda
+    from qlinear.kernels.w8a16_matmul import w8a16_quantize_cuda
+    from qlinear.quantization.int4 import QuantizedLinearInt4
+    from qlinear.quantization.int8 import QuantizedLinearInt8
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    reps = max(5, min(args.steps, 50))
+    stream = torch.cuda.Stream(device=dev)
+    peak, peak_kind = measured_peaks()
+    detail = {}
+    tot_bytes = tot_s = 0.0
+    launches_total = 0
+    for wbits in (4, 8):
+        layers = []
+        for _ in range(DECODE_LAYERS):
+            mods = {}
+            for name, K, N, has_bias in DECODE_LINEARS:
+                w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).half()
+                bias = (torch.randn(N, generator=gen, device=dev) * 0.02).half() if has_bias else None
+                if wbits == 4:
+                    mods[name] = QuantizedLinearInt4(*w4a16_quantize_cuda(w), bias)
+                else:
+                    mods[name] = QuantizedLinearInt8(*w8a16_quantize_cuda(w), bias)
+                del w
+            mods["qkv"] = QuantizedQKV.from_quantized(mods["q"], mods["k"], mods["v"])
+            mods["mlp"] = QuantizedGateUpSiLU.from_quantized(mods["gate"], mods["up"])
+            layers.append(mods)
+
+        def step_unfused(x):
+            for L in layers:
+                q = L["q"](x)
+                L["k"](x)
+                L["v"](x)
+                L["o"](q)
+                g = L["gate"](x)
+                L["up"](x)
+                L["down"](g)
+
+        def step_fused(x):
+            for L in layers:
+                q, _, _ = L["qkv"](x)
+                L["o"](q)
+                L["down"](L["mlp"](x))
+
+        for M in DECODE_MS:
+            x = torch.randn(M, 1536, generator=gen, device=dev).half()
+            row = {}
+            for fused, fn, nl in ((False, step_unfused, 7), (True, step_fused, 4)):
+                with torch.cuda.stream(stream):
+                    fn(x)                                  # eager: sizes the workspaces
+                    torch.cuda.synchronize(dev)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        fn(x)
+                    for _ in range(max(3, args.warmup)):
+                        g.replay()
+                    torch.cuda.synchronize(dev)
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(reps):
+                        g.replay()
+                    e1.record(stream)
+                    torch.cuda.synchronize(dev)
+                t = e0.elapsed_time(e1) * 1e-3 / reps
+                del g
+                nb = decode_step_bytes(wbits, M, fused)
+                key = "fused" if fused else "unfused"
+                row[f"{key}_us"] = round(t * 1e6, 1)
+                row[f"{key}_GBps"] = round(nb / t / 1e9, 1)
+                row[f"{key}_launches"] = nl * DECODE_LAYERS
+                if fused:
+                    tot_bytes += nb
+                    tot_s += t
+                    launches_total += nl * DECODE_LAYERS * reps
+            row["speedup_fused"] = round(row["unfused_us"] / row["fused_us"], 3)
+            detail[f"w{wbits}_M{M}"] = row
+            print(f"[decode_step] w{wbits} M={M}: {row}", file=sys.stderr, flush=True)
+            del x
+        del layers
+        torch.cuda.empty_cache()
+    from qlinear import _lib
+    dev_err = _lib.device_error()
+    if dev_err != 0:
+        raise RuntimeError(f"device error word {dev_err} after the decode-step workload")
+    value = tot_bytes / tot_s / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": max(3, args.warmup),
+        "ms_per_step": tot_s * 1e3 / (2 * len(DECODE_MS)), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config2: decode step of a random-init Qwen2.5-1.5B, 28 layers x q/k/v/o/gate/up/"
+                               "down (q/k/v biased), W4A16 and W8A16, M in {1,4,16,64}; value over the fused "
+                               "path (q/k/v one launch, gate+up with SwiGLU one launch)",
+                   "weight_bytes_per_step": {"w4": DECODE_LAYERS * sum(linear_weight_bytes(4, K, N, b)
+                                                                       for _, K, N, b in DECODE_LINEARS),
+                                             "w8": DECODE_LAYERS * sum(linear_weight_bytes(8, K, N, b)
+                                                                       for _, K, N, b in DECODE_LINEARS)},
+                   "l2": "inputs larger than L2 (one step streams 676 MB / 1.31 GB of distinct weights)"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                     "peak_kind": peak_kind},
+        "gpu_launches": launches_total,
+        "detail": detail}), flush=True)
     return 0
 
 
@@ -699,7 +857,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("config1", "prefill", "sharded"), default="config1")
+    ap.add_argument("--workload", choices=("config1", "decode_step", "prefill", "sharded"), default="config1")
     ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
                     help="a few eager launches of one layer shape (small case for ncu)")
     ap.add_argument("--path", choices=("auto", "gemv", "gemm"), default="auto",
@@ -711,6 +869,8 @@ def main():
         return run_prefill(args)
     if args.workload == "sharded" and args.impl == "ours":
         return run_sharded(args)
+    if args.workload == "decode_step" and args.impl == "ours":
+        return run_decode_step(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

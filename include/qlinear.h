@@ -265,6 +265,25 @@ int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int
                            int rank, int world, int max_m, void* const* peers, int64_t* out,
                            void* stream);
 
+/* Greedy head in ONE launch per rank: the quantized linear (arguments as
+ * ql_w{8,4}a16_linear, minus out/ldo/workspace) of this rank's column shard
+ * followed by the exchange above, fused — the decode kernel turns its
+ * fp16-rounded outputs into argmax keys in its epilogue and its last CTA
+ * runs the exchange; no logits are written.  out_ids[m] = the global argmax
+ * column, identical to ql_w{8,4}a16_linear + ql_argmax_exchange_f16.
+ * Shapes with more than 8 rows, that need a K-split, or with unaligned
+ * operands return QL_ERR_UNSUPPORTED without launching:
+ * ql_linear_argmax_supported(wbits, M, N, K) tells in advance (1 = fused). */
+int ql_w8a16_linear_argmax(const void* x, int x_dtype, const void* w_q, const void* scale, int scale_dtype,
+                           const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                           int64_t ldx, int64_t ldw, int64_t col_offset, int rank, int world, int max_m,
+                           void* const* peers, int64_t* out_ids, unsigned flags, void* stream);
+int ql_w4a16_linear_argmax(const void* x, int x_dtype, const void* w_packed, int layout, const void* scales,
+                           const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                           int64_t ldx, int64_t ldw, int64_t lds, int64_t col_offset, int rank, int world,
+                           int max_m, void* const* peers, int64_t* out_ids, unsigned flags, void* stream);
+int ql_linear_argmax_supported(int wbits, int64_t M, int64_t N, int64_t K);
+
 /* ------------------------------------------------------------- diagnostics */
 const char* ql_strerror(int status);
 /* Version as (major << 16) | (minor << 8) | patch. */

@@ -40,9 +40,15 @@
 //     counter) sums the slots in slot order, applies scale/bias and zeroes
 //     slots and counter, so the result is deterministic and the workspace
 //     stays zeroed.
+//   * Greedy-head mode (amax.out set, K unsplit, M <= 8): instead of storing the
+//     outputs, each tile turns its fp16-rounded outputs into argmax keys
+//     (qargmax.cuh), the CTA keeps the per-row maximum in shared memory and
+//     merges it into the exchange buffer's scratch once; the last CTA of the
+//     grid runs the exchange over NVLink (qxchg.cuh) and writes the argmax
+//     columns.  One launch per rank for logits-free greedy decoding.
 #pragma once
 
-#include "ql_common.cuh"
+#include "qxchg.cuh"
 
 namespace ql {
 namespace gemv {
@@ -83,6 +89,7 @@ struct Params {
                           // tiles and stores silu(gate) * up, [M, n] (ks == 1 only)
   uint32_t* counters;     // [gridDim.z * nblk] (ks > 1)
   float* partials;        // [gridDim.z][nblk][ks][mc][tpc*16] (ks > 1)
+  xchg::Ctx amax;         // amax.out != nullptr: greedy-head mode (ks == 1, swiglu_n == 0)
   unsigned* err;          // device error word
 };
 
@@ -107,7 +114,8 @@ __host__ __device__ inline Smem smem_layout(int wbits, int mc, int x_rows, int t
   s.red = align_up((size_t)tpc * wpt * kTileRows * mc * 4, 128);
   s.x = align_up((size_t)x_rows * x_stride * 2, 16);
   s.sc = (wbits == 4 && !scale_tma) ? align_up((size_t)kb_per_split * 2 * tpc * kTileRows * 4, 16) : 0;
-  s.bars = align_up((size_t)2 * stages * 8 + 16, 16);
+  // mbarriers, last_flag + abort, the CTA's row maxima (greedy-head mode)
+  s.bars = align_up((size_t)2 * stages * 8 + 16 + (size_t)8 * mc, 16);
   s.total = 128 /* base alignment slack */ + s.ring + s.red + s.x + s.sc + s.bars;
   return s;
 }
@@ -304,6 +312,8 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   uint64_t* empty = full + stages;
   int* last_flag = reinterpret_cast<int*>(empty + stages);
   volatile int* abort = last_flag + 1;    // set once a wait of this CTA gives up
+  unsigned long long* amax_s = reinterpret_cast<unsigned long long*>(empty + stages + 2);   // [MC]
+  const bool greedy = MT == 1 && p.amax.out != nullptr;   // host: greedy-head plans have MT == 1
 
   const int split = blockIdx.y, mchunk = blockIdx.z;
   const int kb0 = split * p.kb_per_split;
@@ -418,6 +428,8 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
         *reinterpret_cast<uint4*>(srow + v * 8) = val;
       }
     }
+    if (greedy)
+      for (int i = ctid; i < MC; i += nct) amax_s[i] = 0ull;
   }
   named_bar_sync(1, nct);
   griddep_launch_dependents();
@@ -534,12 +546,35 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       // Only the warps of one tile meet here (named barrier 2 + tt), so
       // tiles finish their blocks independently.
       if (wpt > 1) named_bar_sync(2 + tt, wpt * 32); else __syncwarp();
-      for (int idx = w * 32 + lane; idx < mvalid * kTileRows; idx += wpt * 32) {
-        const int m = idx >> 4, rr = idx & 15;
-        float v = 0.f;
-        for (int w2 = 0; w2 < wpt; ++w2) v += red[((tt * wpt + w2) * MC + m) * kTileRows + rr];
-        const int n = row0 + tt * kTileRows + rr;
-        if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+      if (greedy) {
+        // keys of the fp16-rounded outputs (what argmax over the stored
+        // logits would see); max over the tile's 16 rows within each half
+        // warp, then into the CTA's row maxima
+        for (int b = w * 32; b < mvalid * kTileRows; b += wpt * 32) {   // warp-uniform
+          const int idx = b + lane;
+          unsigned long long key = 0ull;
+          if (idx < mvalid * kTileRows) {
+            const int m = idx >> 4, rr = idx & 15;
+            float v = 0.f;
+            for (int w2 = 0; w2 < wpt; ++w2) v += red[((tt * wpt + w2) * MC + m) * kTileRows + rr];
+            const int n = row0 + tt * kTileRows + rr;
+            if (n < p.N) {
+              const __half h = __float2half_rn(finish_value<WBITS>(p, v, n));
+              key = amax::row_key(__half_as_ushort(h), p.amax.col_offset + n);
+            }
+          }
+          #pragma unroll
+          for (int o = 8; o > 0; o >>= 1) key = amax::umax64(key, __shfl_xor_sync(0xffffffffu, key, o));
+          if ((lane & 15) == 0 && idx < mvalid * kTileRows) atomicMax(amax_s + (idx >> 4), key);
+        }
+      } else {
+        for (int idx = w * 32 + lane; idx < mvalid * kTileRows; idx += wpt * 32) {
+          const int m = idx >> 4, rr = idx & 15;
+          float v = 0.f;
+          for (int w2 = 0; w2 < wpt; ++w2) v += red[((tt * wpt + w2) * MC + m) * kTileRows + rr];
+          const int n = row0 + tt * kTileRows + rr;
+          if (n < p.N) p.out[(long long)(m0 + m) * p.ldo + n] = __float2half_rn(finish_value<WBITS>(p, v, n));
+        }
       }
       if (wpt > 1) named_bar_sync(2 + tt, wpt * 32); else __syncwarp();   // red is reused next block
       if (WBITS == 4 && !scale_tma) named_bar_sync(1, nct);               // so are the block scales
@@ -592,6 +627,18 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       }
       named_bar_sync(1, nct);   // red, the block scales and last_flag are reused by the next block
     }
+  }
+
+  if (greedy) {
+    // the CTA's row maxima -> this rank's scratch; the last CTA of the grid
+    // exchanges the keys with the other ranks and writes the columns
+    named_bar_sync(1, nct);
+    unsigned long long* scratch = xchg::scratch_of(p.amax);
+    for (int i = ctid; i < mvalid; i += nct) atomicMax(scratch + m0 + i, amax_s[i]);
+    named_bar_sync(1, nct);
+    if (ctid == 0) *last_flag = xchg::arrive_last(p.amax, gridDim.x * gridDim.y * gridDim.z) ? 1 : 0;
+    named_bar_sync(1, nct);
+    if (*last_flag) xchg::publish_and_combine(p.amax, p.M, ctid, nct, p.err, [&] { named_bar_sync(1, nct); });
   }
 }
 

@@ -404,6 +404,7 @@ struct LinearArgs {
   unsigned flags;
   cudaStream_t stream;
   int64_t swiglu_n = 0;   // > 0: fused gate+up, N = 2 * swiglu_n stacked weight rows
+  const ql::xchg::Ctx* amax = nullptr;   // greedy head: argmax columns instead of outputs
 };
 
 int run_generic(const LinearArgs& a) {
@@ -484,6 +485,11 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
   const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
   p.early_weights = pdl ? 1 : 0;
   p.swiglu_n = (int)a.swiglu_n;
+  std::memset(&p.amax, 0, sizeof(p.amax));
+  if (a.amax) {
+    if (pl.ks != 1 || pl.mt != 1 || a.swiglu_n > 0) return QL_ERR_UNSUPPORTED;
+    p.amax = *a.amax;
+  }
   p.err = dev->err_word;
   if (pl.ks > 1) {
     const size_t counters = ((size_t)pl.nblk * pl.mchunks * 4 + 255) / 256 * 256;
@@ -741,6 +747,62 @@ int run_swiglu(const LinearArgs& a) {
                 static_cast<__half*>(a.out), (long long)a.ldo);
 }
 
+// Exchange context of one call; QL_OK or the status for bad arguments.
+int make_xchg_ctx(ql::xchg::Ctx* c, int64_t col_offset, int rank, int world, int max_m, void* const* peers,
+                  int64_t* out) {
+  if (!peers || !out) return QL_ERR_NULL_POINTER;
+  if (world < 1 || world > QL_XCHG_MAX_RANKS || rank < 0 || rank >= world || max_m < 1 || max_m > 65535 ||
+      col_offset < 0)
+    return QL_ERR_BAD_SHAPE;
+  std::memset(c, 0, sizeof(*c));
+  for (int q = 0; q < world; ++q) {
+    c->peer[q] = static_cast<unsigned char*>(peers[q]);
+    if (!c->peer[q]) return QL_ERR_NULL_POINTER;
+  }
+  c->out = reinterpret_cast<long long*>(out);
+  c->col_offset = col_offset;
+  c->rank = rank;
+  c->world = world;
+  c->max_m = max_m;
+  return QL_OK;
+}
+
+// Greedy head in one launch: the decode kernel with an unsplit K turns its
+// outputs into argmax keys and runs the exchange itself.  Shapes that take
+// the tensor-core path, have more than 8 rows, or have no unsplit decode plan, are
+// QL_ERR_UNSUPPORTED (the caller runs the linear, then ql_argmax_exchange_f16).
+bool greedy_fused_plan(int wbits, int64_t M, int64_t N, int64_t K, int sms, int scale_tma) {
+  if (use_gemm(wbits, M, N, K)) return false;
+  GemvPlan pl;
+  return plan_gemv(wbits, M, N, K, sms, 0, scale_tma, &pl) && pl.ks == 1 && pl.mt == 1;
+}
+
+int run_linear_argmax(const LinearArgs& a0, int64_t col_offset, int rank, int world, int max_m, void* const* peers,
+                      int64_t* out_ids) {
+  if (!a0.x || !a0.w || !a0.scale) return QL_ERR_NULL_POINTER;
+  ql::xchg::Ctx c;
+  int st = make_xchg_ctx(&c, col_offset, rank, world, max_m, peers, out_ids);
+  if (st != QL_OK) return st;
+  if (a0.M < 1 || a0.M > max_m || a0.N < 1 || a0.N > INT_MAX || a0.K < 1 || a0.K > INT_MAX ||
+      col_offset + a0.N > 0xFFFFFFFFLL)
+    return QL_ERR_BAD_SHAPE;
+  LinearArgs a = a0;
+  a.ldo = a.N;
+  a.out = const_cast<void*>(a.x);   // never written in greedy-head mode; satisfies the common checks
+  bool empty;
+  st = check_args(a, a.N, &empty);
+  if (st != QL_OK) return st;
+  if (!fast_path_ok(a)) return QL_ERR_UNSUPPORTED;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  const int scale_tma = (a.wbits == 4 && aligned16(a.scale) && a.lds % 8 == 0) ? 1 : 0;
+  if (!greedy_fused_plan(a.wbits, a.M, a.N, a.K, dev->sms, scale_tma)) return QL_ERR_UNSUPPORTED;
+  a.ws = nullptr;
+  a.ws_bytes = 0;
+  a.amax = &c;
+  return run_gemv(a, dev);
+}
+
 }  // namespace
 
 // ======================================================================
@@ -764,6 +826,37 @@ int ql_w4a16_linear(const void* x, int x_dtype, const void* w_packed, int layout
   LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, out, M, N, K, ldx, ldw, lds,
                ldo, workspace, workspace_bytes, flags, static_cast<cudaStream_t>(stream)};
   return run_linear(a);
+}
+
+int ql_w8a16_linear_argmax(const void* x, int x_dtype, const void* w_q, const void* scale, int scale_dtype,
+                           const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                           int64_t col_offset, int rank, int world, int max_m, void* const* peers, int64_t* out_ids,
+                           unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  LinearArgs a{8, x, w_q, 0, scale, scale_dtype, bias, bias_dtype, nullptr, M, N, K, ldx, ldw, 0, N,
+               nullptr, 0, flags, static_cast<cudaStream_t>(stream)};
+  return run_linear_argmax(a, col_offset, rank, world, max_m, peers, out_ids);
+}
+
+int ql_w4a16_linear_argmax(const void* x, int x_dtype, const void* w_packed, int layout, const void* scales,
+                           const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                           int64_t lds, int64_t col_offset, int rank, int world, int max_m, void* const* peers,
+                           int64_t* out_ids, unsigned flags, void* stream) {
+  if (x_dtype != QL_DTYPE_F16) return QL_ERR_UNSUPPORTED;
+  LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, nullptr, M, N, K, ldx, ldw, lds,
+               N, nullptr, 0, flags, static_cast<cudaStream_t>(stream)};
+  return run_linear_argmax(a, col_offset, rank, world, max_m, peers, out_ids);
+}
+
+int ql_linear_argmax_supported(int wbits, int64_t M, int64_t N, int64_t K) {
+  if ((wbits != 4 && wbits != 8) || M < 1 || N < 1 || K < 1 || M > INT_MAX || N > INT_MAX || K > INT_MAX) return 0;
+  if (wbits == 4 && K % 128 != 0) return 0;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return 0;
+  // int4 scales may or may not qualify for TMA (alignment): both plans must be unsplit
+  return greedy_fused_plan(wbits, M, N, K, dev->sms, 0) && (wbits == 8 || greedy_fused_plan(wbits, M, N, K, dev->sms, 1))
+             ? 1 : 0;
 }
 
 int ql_w8a16_gate_up_silu(const void* x, int x_dtype, const void* w_q, const void* scale, int scale_dtype,
@@ -1023,15 +1116,8 @@ int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int
   p.N = (int)N;
   p.span = 8192;
   p.vec = aligned16(x) && ldx % 8 == 0 && N % 8 == 0;
-  p.col_offset = col_offset;
-  p.rank = rank;
-  p.world = world;
-  p.max_m = max_m;
-  for (int q = 0; q < ql::xchg::kMaxRanks; ++q) {
-    p.peer[q] = q < world ? static_cast<unsigned char*>(peers[q]) : nullptr;
-    if (q < world && !p.peer[q]) return QL_ERR_NULL_POINTER;
-  }
-  p.out = reinterpret_cast<long long*>(out);
+  st = make_xchg_ctx(&p.c, col_offset, rank, world, max_m, peers, out);
+  if (st != QL_OK) return st;
   p.err = dev->err_word;
   return launch(ql::xchg::argmax_exchange_kernel, dim3((unsigned)cdiv(N, p.span), (unsigned)M), dim3(256), 0,
                 static_cast<cudaStream_t>(stream), true, p);

@@ -18,6 +18,10 @@
 // of the largest key.  A rank can be at most one call ahead of another (it
 // needs everybody's keys of the call before), so two banks by epoch parity
 // are enough.  Ranks must make the same sequence of calls.
+//
+// The decode GEMV (qgemv.cuh) runs the same protocol from its own epilogue
+// (keys of the fp16-rounded outputs, no logits written): `Ctx` is the part
+// both kernels share and `publish_and_combine` the last CTA's step.
 #pragma once
 
 #include "qargmax.cuh"
@@ -39,14 +43,19 @@ __host__ __device__ inline Layout layout(int world, int max_m) {
   return l;
 }
 
+// What a kernel needs to take part in one exchange.
+struct Ctx {
+  unsigned char* peer[kMaxRanks];   // exchange buffer of every rank (peer[rank] = own)
+  long long* out;                   // [M] argmax columns
+  long long col_offset;             // global column of this rank's first column
+  int rank, world, max_m;
+};
+
 struct Params {
   const __half* x;
   long long ldx;
   int M, N, span, vec;
-  long long col_offset;
-  int rank, world, max_m;
-  unsigned char* peer[kMaxRanks];   // exchange buffer of every rank (peer[rank] = own)
-  long long* out;                   // [M] argmax columns
+  Ctx c;
   unsigned* err;
 };
 
@@ -58,12 +67,71 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned 
 }
 constexpr unsigned long long kKeyMask = 0xFFFFFFFFFFFFull;   // the 48 key bits
 
-__global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
-  const Layout L = layout(p.world, p.max_m);
-  unsigned char* own = p.peer[p.rank];
+// This rank's row maxima (scratch) are complete: push them, tagged with the
+// call's epoch, into every rank's bank, wait (bounded) for every rank's,
+// write the argmax columns and reset scratch, the CTA counter and the epoch
+// for the next call.  Run by all `nthr` threads of the last CTA; `bar`
+// synchronises them.
+template <class Bar>
+__device__ __forceinline__ void publish_and_combine(const Ctx& c, int M, int tid, int nthr, unsigned* err, Bar bar) {
+  const Layout L = layout(c.world, c.max_m);
+  unsigned char* own = c.peer[c.rank];
   unsigned long long* scratch = reinterpret_cast<unsigned long long*>(own + L.scratch);
   unsigned* counter = reinterpret_cast<unsigned*>(own + L.state);
   unsigned* epoch_done = counter + 1;
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_done) + 1u;
+  const int bank = (int)(e & 1u);
+  const unsigned long long tag = (unsigned long long)((e & 0x7FFFu) | 0x8000u) << 48;   // never 0
+  for (int q = 0; q < c.world; ++q) {
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(c.peer[q] + L.keys) + ((size_t)bank * c.world + c.rank) * c.max_m;
+    for (int i = tid; i < M; i += nthr) st_volatile_u64(dst + i, tag | ld_volatile_u64(scratch + i));
+  }
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(own + L.keys) + (size_t)bank * c.world * c.max_m;
+  for (int i = tid; i < M; i += nthr) {
+    unsigned long long b = 0ull;
+    for (int q = 0; q < c.world; ++q) {
+      const unsigned long long* slot = keys + (size_t)q * c.max_m + i;
+      unsigned long long v = ld_volatile_u64(slot);
+      if ((v & ~kKeyMask) != tag) {               // bounded wait for rank q's key of this call
+        const long long t0 = clock64();
+        while (((v = ld_volatile_u64(slot)) & ~kKeyMask) != tag) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            atomicCAS(err, 0u, kDevErrPeerWait);
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      b = amax::umax64(b, v & kKeyMask);
+    }
+    c.out[i] = (long long)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull));
+    scratch[i] = 0ull;                       // ready for the next call
+  }
+  bar();
+  if (tid == 0) {
+    *counter = 0u;
+    *reinterpret_cast<volatile unsigned*>(epoch_done) = e;
+  }
+}
+
+// This CTA's contribution is in scratch: count the CTA in; true for the
+// last one to arrive (which then sees every CTA's atomics).  Thread 0 only.
+__device__ __forceinline__ bool arrive_last(const Ctx& c, unsigned total) {
+  const Layout L = layout(c.world, c.max_m);
+  unsigned* counter = reinterpret_cast<unsigned*>(c.peer[c.rank] + L.state);
+  __threadfence();
+  const bool last = atomicAdd(counter, 1u) == total - 1;
+  if (last) __threadfence();
+  return last;
+}
+
+__device__ __forceinline__ unsigned long long* scratch_of(const Ctx& c) {
+  return reinterpret_cast<unsigned long long*>(c.peer[c.rank] + layout(c.world, c.max_m).scratch);
+}
+
+__global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
+  unsigned long long* scratch = scratch_of(p.c);
   __shared__ unsigned long long red[8];
   __shared__ int is_last;
 
@@ -83,12 +151,12 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
       const unsigned w[4] = {v.x, v.y, v.z, v.w};
       #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] & 0xFFFFu), p.col_offset + c + 2 * j));
-        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] >> 16), p.col_offset + c + 2 * j + 1));
+        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] & 0xFFFFu), p.c.col_offset + c + 2 * j));
+        best = amax::umax64(best, amax::row_key((unsigned short)(w[j] >> 16), p.c.col_offset + c + 2 * j + 1));
       }
     }
   } else {
-    for (int c = c0 + (int)threadIdx.x; c < c1; c += 256) best = amax::umax64(best, amax::row_key(row[c], p.col_offset + c));
+    for (int c = c0 + (int)threadIdx.x; c < c1; c += 256) best = amax::umax64(best, amax::row_key(row[c], p.c.col_offset + c));
   }
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = amax::umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
@@ -98,49 +166,13 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
     unsigned long long b = red[0];
     for (int w = 1; w < 8; ++w) b = amax::umax64(b, red[w]);
     atomicMax(scratch + m, b);
-    __threadfence();
-    const unsigned total = gridDim.x * gridDim.y;
-    is_last = atomicAdd(counter, 1u) == total - 1;
-    if (is_last) __threadfence();
+    is_last = arrive_last(p.c, gridDim.x * gridDim.y);
   }
   __syncthreads();
   if (!is_last) return;
 
   // ---- last CTA: push tagged keys, wait for every rank's, combine
-  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_done) + 1u;
-  const int bank = (int)(e & 1u);
-  const unsigned long long tag = (unsigned long long)((e & 0x7FFFu) | 0x8000u) << 48;   // never 0
-  for (int q = 0; q < p.world; ++q) {
-    unsigned long long* dst =
-        reinterpret_cast<unsigned long long*>(p.peer[q] + L.keys) + ((size_t)bank * p.world + p.rank) * p.max_m;
-    for (int i = threadIdx.x; i < p.M; i += blockDim.x) st_volatile_u64(dst + i, tag | ld_volatile_u64(scratch + i));
-  }
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(own + L.keys) + (size_t)bank * p.world * p.max_m;
-  for (int i = threadIdx.x; i < p.M; i += blockDim.x) {
-    unsigned long long b = 0ull;
-    for (int q = 0; q < p.world; ++q) {
-      const unsigned long long* slot = keys + (size_t)q * p.max_m + i;
-      unsigned long long v = ld_volatile_u64(slot);
-      if ((v & ~kKeyMask) != tag) {               // bounded wait for rank q's key of this call
-        const long long t0 = clock64();
-        while (((v = ld_volatile_u64(slot)) & ~kKeyMask) != tag) {
-          if (clock64() - t0 > kWaitBudgetCycles) {
-            atomicCAS(p.err, 0u, kDevErrPeerWait);
-            break;
-          }
-          __nanosleep(32);
-        }
-      }
-      b = amax::umax64(b, v & kKeyMask);
-    }
-    p.out[i] = (long long)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull));
-    scratch[i] = 0ull;                       // ready for the next call
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    *counter = 0u;
-    *reinterpret_cast<volatile unsigned*>(epoch_done) = e;
-  }
+  publish_and_combine(p.c, p.M, (int)threadIdx.x, (int)blockDim.x, p.err, [] { __syncthreads(); });
 }
 
 }  // namespace xchg

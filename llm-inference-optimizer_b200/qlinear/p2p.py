@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .kernels._launch import default_flags, dtype_code, ld, on_device, ptr
 
 
 class PeerExchange:
@@ -73,6 +74,50 @@ class PeerExchange:
         _lib.check(_lib.load().ql_argmax_exchange_f16(
             logits.data_ptr(), M, N, ldx, col_offset, self.rank, self.world, self.max_m, self._peers,
             out.data_ptr(), stream.cuda_stream))
+        return out
+
+    def linear_argmax(self, x: torch.Tensor, module, col_offset: int) -> Optional[torch.Tensor]:
+        """Global argmax column of every row of ``module(x)`` (this rank's
+        column shard starting at `col_offset`) in ONE launch: the decode
+        kernel reduces its fp16-rounded outputs to keys in its epilogue and
+        its last CTA runs the exchange — the logits are never written.
+        Returns None (nothing launched) for shapes the fused kernel does not
+        take (more than 8 rows, K-split plans, tensor-core shapes, unaligned
+        operands); the caller then runs the linear and ``argmax``."""
+        from .quantization.int4 import QuantizedLinearInt4
+        from .quantization.int8 import QuantizedLinearInt8
+        assert x.is_cuda and x.dtype == torch.float16
+        K = module.in_features
+        x2 = x.reshape(-1, K)
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        M, N = x2.shape[0], module.out_features
+        if not 1 <= M <= self.max_m:
+            return None
+        lib = _lib.load()
+        wbits = 4 if isinstance(module, QuantizedLinearInt4) else 8 if isinstance(module, QuantizedLinearInt8) else 0
+        if wbits == 0 or not lib.ql_linear_argmax_supported(wbits, M, N, K):
+            return None
+        out = torch.empty(M, dtype=torch.int64, device=x.device)
+        bias = module.bias
+        bias_dt = dtype_code(bias.dtype) if bias is not None else 0
+        with on_device(x.device):
+            stream = torch.cuda.current_stream(x.device).cuda_stream
+            if wbits == 4:
+                w, sc = module.weight_packed, module.scales
+                st = lib.ql_w4a16_linear_argmax(
+                    ptr(x2), _lib.QL_DTYPE_F16, ptr(w), module.layout, ptr(sc), ptr(bias), bias_dt, M, N, K,
+                    ld(x2, K), ld(w, K // 2), ld(sc, N), col_offset, self.rank, self.world, self.max_m,
+                    self._peers, ptr(out), default_flags(), stream)
+            else:
+                w, sc = module.weight_q, module.scale
+                st = lib.ql_w8a16_linear_argmax(
+                    ptr(x2), _lib.QL_DTYPE_F16, ptr(w), ptr(sc), dtype_code(sc.dtype), ptr(bias), bias_dt, M, N,
+                    K, ld(x2, K), ld(w, K), col_offset, self.rank, self.world, self.max_m, self._peers, ptr(out),
+                    default_flags(), stream)
+        if st == _lib.QL_ERR_UNSUPPORTED:
+            return None
+        _lib.check(st)
         return out
 
     def close(self) -> None:

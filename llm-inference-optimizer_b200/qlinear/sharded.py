@@ -151,20 +151,26 @@ class ShardedQuantizedLinear(nn.Module):
         full = full.reshape(M, self.groups, self.world * self.block)[:, :, :n]
         return full.reshape(M, self.out_features)
 
-    def argmax(self, x: torch.Tensor) -> torch.Tensor:
+    def argmax(self, x: torch.Tensor, fused: bool = True) -> torch.Tensor:
         """argmax over the full output row, without gathering the outputs.
 
         Each rank reduces its columns to one key per row (value, global
         column; ties to the smallest column, as torch.argmax), the ranks
         exchange the keys (8 bytes per row and rank) and every rank takes the
-        max: with an attached PeerExchange in one kernel over NVLink, else
-        through an NCCL all-gather.  Equals torch.argmax(self(x), dim=-1).
-        groups == 1 only."""
+        max: with an attached PeerExchange in one kernel over NVLink (for
+        decode-sized batches the shard's linear itself, whose epilogue makes
+        the keys: one launch per rank and no logits), else through an NCCL
+        all-gather.  Equals torch.argmax(self(x), dim=-1).  groups == 1 only;
+        fused=False keeps the linear and the exchange as two launches."""
         assert self.groups == 1, "argmax is defined for a single output block"
         K = self.in_features
         x2 = x.reshape(-1, K)
-        y = self.local_fn(self.local, x2)                       # [M, widths[rank]]
         lo = shard_bounds(self.out_features, self.rank, self.world)[0]
+        if fused and self.exchange is not None and self.local_fn is local_linear_cuda:
+            ids = self.exchange.linear_argmax(x2, self.local, lo)
+            if ids is not None:
+                return ids.reshape(x.shape[:-1])
+        y = self.local_fn(self.local, x2)                       # [M, widths[rank]]
         if self.exchange is not None:                           # one kernel, keys over NVLink
             return self.exchange.argmax(y, lo).reshape(x.shape[:-1])
         keys = self.key_fn(y, lo)                               # [M] int64 key bits

@@ -34,3 +34,26 @@ def assert_parity(y_gpu: torch.Tensor, y_ref_f32: np.ndarray, x: np.ndarray, w_d
     ok, max_abs, rel, b_abs, b_rel = orc.check_parity(y, y_ref_f32, x, w_deq)
     assert ok, f"{what}: max_abs {max_abs:.3e} (bound {b_abs:.3e}) rel_l2 {rel:.3e} (bound {b_rel:.1e})"
     return max_abs, rel
+
+
+def linear_unsplit(q, x):
+    """q(x) through the decode kernel planned without a workspace (no
+    K-split): the plan the fused greedy-head launch uses, so its fp16
+    outputs are bit-identical to what that launch reduces."""
+    from qlinear import _lib
+    from qlinear.quantization.int8 import QuantizedLinearInt8
+    lib = _lib.load()
+    M, K = x.shape
+    N = q.out_features
+    out = torch.empty(M, N, dtype=torch.float16, device=x.device)
+    flags = _lib.QL_FLAG_FORCE_GEMV | _lib.QL_FLAG_PDL
+    stream = torch.cuda.current_stream().cuda_stream
+    bias = q.bias.data_ptr() if q.bias is not None else None
+    if isinstance(q, QuantizedLinearInt8):
+        st = lib.ql_w8a16_linear(x.data_ptr(), 0, q.weight_q.data_ptr(), q.scale.data_ptr(), _lib.QL_DTYPE_F32,
+                                 bias, 0, out.data_ptr(), M, N, K, K, K, N, None, 0, flags, stream)
+    else:
+        st = lib.ql_w4a16_linear(x.data_ptr(), 0, q.weight_packed.data_ptr(), q.layout, q.scales.data_ptr(), bias,
+                                 0, out.data_ptr(), M, N, K, K, K // 2, N, N, None, 0, flags, stream)
+    _lib.check(st)
+    return out

@@ -77,6 +77,37 @@ def test_host_argument_checks_without_gpu():
     assert st == _lib.QL_ERR_UNSUPPORTED
 
 
+def test_greedy_head_argument_checks_without_gpu():
+    """The fused linear + argmax entry points check the exchange arguments
+    and shapes on the host; the support query answers 0 without a device."""
+    import ctypes
+    lib = _lib.load()
+    peers = (ctypes.c_void_p * 2)(1, 1)
+    # world outside 1..8
+    st = lib.ql_w4a16_linear_argmax(1, 0, 1, 0, 1, None, 0, 1, 16, 128, 128, 64, 16, 0, 0, 9, 4, peers, 1, 0, None)
+    assert st == _lib.QL_ERR_BAD_SHAPE
+    # rows beyond the exchange's max_m
+    st = lib.ql_w8a16_linear_argmax(1, 0, 1, 1, 1, None, 0, 5, 16, 128, 128, 128, 0, 0, 2, 4, peers, 1, 0, None)
+    assert st == _lib.QL_ERR_BAD_SHAPE
+    # missing peer buffer / output
+    null_peers = (ctypes.c_void_p * 2)(1, None)
+    st = lib.ql_w8a16_linear_argmax(1, 0, 1, 1, 1, None, 0, 1, 16, 128, 128, 128, 0, 0, 2, 4, null_peers, 1, 0,
+                                    None)
+    assert st == _lib.QL_ERR_NULL_POINTER
+    st = lib.ql_w8a16_linear_argmax(1, 0, 1, 1, 1, None, 0, 1, 16, 128, 128, 128, 0, 0, 2, 4, peers, None, 0, None)
+    assert st == _lib.QL_ERR_NULL_POINTER
+    # columns past 2^32 - 1
+    st = lib.ql_w8a16_linear_argmax(1, 0, 1, 1, 1, None, 0, 1, 16, 128, 128, 128, 0xFFFFFFFF, 0, 2, 4, peers, 1,
+                                    0, None)
+    assert st == _lib.QL_ERR_BAD_SHAPE
+    # bf16 activations
+    st = lib.ql_w8a16_linear_argmax(1, 2, 1, 1, 1, None, 0, 1, 16, 128, 128, 128, 0, 0, 2, 4, peers, 1, 0, None)
+    assert st == _lib.QL_ERR_UNSUPPORTED
+    assert lib.ql_linear_argmax_supported(4, 1, 4096, 1536) in (0, 1)
+    assert lib.ql_linear_argmax_supported(5, 1, 4096, 1536) == 0
+    assert lib.ql_linear_argmax_supported(4, 1, 4096, 100) == 0
+
+
 def test_pack_unpack_roundtrip():
     """The reference's KAT (tests/test_w4a16_kernel.py:52-59)."""
     torch.manual_seed(0)

@@ -11,7 +11,7 @@ from qlinear.kernels.argmax import argmax_f16, argmax_keys, combine_keys, key_co
 from qlinear.quantization.int4 import QuantizedLinearInt4
 from qlinear.sharded import ShardedQuantizedLinear
 
-from helpers import make_linear, make_x
+from helpers import linear_unsplit, make_linear, make_x
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="requires a CUDA GPU")]
@@ -80,6 +80,65 @@ def test_exchange_single_rank_matches_torch_and_replays():
         del graph
         from qlinear import _lib
         assert _lib.device_error() == 0
+    finally:
+        px.close()
+
+
+@pytest.mark.parametrize("wbits,M,K,N,bias,off", [(4, 1, 1536, 18992, False, 0), (4, 3, 1536, 4099, True, 77),
+                                                    (8, 1, 1536, 18992, False, 5), (8, 8, 4096, 16032, True, 0),
+                                                    (4, 8, 4096, 16032, False, 112224)])
+def test_linear_argmax_fused_single_rank(wbits, M, K, N, bias, off):
+    """The decode kernel's greedy-head epilogue (one launch: linear, keys,
+    exchange) equals torch.argmax over the same kernel's fp16 outputs, for
+    both formats, masked tail tiles, bias and column offsets; mixed with the
+    unfused exchange and replayed from a CUDA graph (epochs advance)."""
+    from qlinear import _lib
+    from qlinear.p2p import PeerExchange
+    from qlinear.quantization.int8 import QuantizedLinearInt8
+    lin = make_linear(K, N, bias=bias, std=0.02, seed=N + M)
+    q = (QuantizedLinearInt4 if wbits == 4 else QuantizedLinearInt8).from_linear(lin).cuda()
+    x = make_x(M, K, seed=M + 1).cuda()
+    px = PeerExchange(0, 1, max_m=8)
+    try:
+        assert _lib.load().ql_linear_argmax_supported(wbits, M, N, K) == 1
+        want = torch.argmax(linear_unsplit(q, x), dim=-1) + off
+        got = px.linear_argmax(x, q, off)
+        assert got is not None and torch.equal(got, want)
+        assert torch.equal(px.argmax(linear_unsplit(q, x), off), want)   # unfused exchange in between
+        assert torch.equal(px.linear_argmax(x, q, off), want)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                out = px.linear_argmax(x, q, off)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(4):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+        del graph
+        assert _lib.device_error() == 0
+    finally:
+        px.close()
+
+
+def test_linear_argmax_declines_unfused_shapes():
+    """More than 8 rows (two batch tiles), more rows than the exchange
+    holds, or a tensor-core shape: nothing is launched and None comes back."""
+    from qlinear import _lib
+    from qlinear.p2p import PeerExchange
+    lin = make_linear(1536, 4096, bias=False, std=0.02, seed=2)
+    q = QuantizedLinearInt4.from_linear(lin).cuda()
+    px = PeerExchange(0, 1, max_m=64)
+    try:
+        assert _lib.load().ql_linear_argmax_supported(4, 12, 4096, 1536) == 0
+        assert _lib.load().ql_linear_argmax_supported(4, 64, 4096, 1536) == 0
+        assert px.linear_argmax(make_x(12, 1536, seed=3).cuda(), q, 0) is None
+        assert px.linear_argmax(make_x(64, 1536, seed=3).cuda(), q, 0) is None
+        x = make_x(12, 1536, seed=3).cuda()
+        assert torch.equal(px.argmax(q(x), 0), torch.argmax(q(x), dim=-1))   # the exchange is still in step
     finally:
         px.close()
 

@@ -68,8 +68,14 @@ def _worker(rank, world, port, case, result_q):
         if groups == 1:   # sharded argmax: keys all-gathered, equals argmax of the gathered logits
             want = torch.argmax(y, dim=-1)
             same = same and torch.equal(sh.argmax(xd), want)
-            # the same through the NVLink exchange kernel, eager and from a graph
+            # the same through the NVLink exchange kernel, eager and from a graph;
+            # up to 8 rows the shard's linear runs unsplit with the exchange in its
+            # epilogue, so its expectation is the argmax of the unsplit outputs
+            from helpers import linear_unsplit
             from qlinear.p2p import PeerExchange
+            if M <= 8:
+                ref_sh = ShardedQuantizedLinear(sh.local, sh.out_features, rank, world, local_fn=linear_unsplit)
+                want = torch.argmax(ref_sh(xd), dim=-1)
             sh.exchange = PeerExchange(rank, world, max_m=64)
             same = same and torch.equal(sh.argmax(xd), want)
             with torch.cuda.stream(s):
@@ -94,7 +100,8 @@ def _worker(rank, world, port, case, result_q):
         result_q.put((rank, False, repr(e)[:300], None))
 
 
-@pytest.mark.parametrize("case", [(1536, 8192 + 37, 1, 4, 1), (4096, 2 * 1792, 16, 8, 2), (1536, 4096, 64, 4, 1)])
+@pytest.mark.parametrize("case", [(1536, 8192 + 37, 1, 4, 1), (4096, 2 * 1792, 16, 8, 2), (1536, 4096, 64, 4, 1),
+                                  (4096, 16032 * 2, 3, 8, 1)])
 def test_sharded_nccl_two_gpus(case):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
