@@ -139,6 +139,15 @@ size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes,
                  int64_t* fields, int nfields);
 
+/* The tensor-core kernel's launch plan for (wbits, layout, M, N, K) on the
+ * current device (K % 128 == 0), for tuning and tests: fields[0..7] =
+ * activation rows per tile, K-splits (= thread-block cluster size; the
+ * splits of a tile reduce through distributed shared memory), 128-k stages
+ * per split, shared-memory ring stages, dynamic shared bytes, tiles, CTAs,
+ * clusters of that size the device holds at once (0 without a split)
+ * (nfields >= 8).  No counterpart in the reference. */
+int ql_gemm_plan(int wbits, int layout, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields);
+
 /* ----------------------------------------------- no-allocation variant */
 /* Size of the fixed scratch array behind ql_w4a16_linear_static_ws. */
 #define QL_STATIC_WS_BYTES (2u * 1024u * 1024u)

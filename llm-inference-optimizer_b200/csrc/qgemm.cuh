@@ -24,7 +24,16 @@
 //   * epilogue (warps 2-9, each half of the activation columns): tcgen05.ld
 //     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
-// Per-CTA TMA loads only; every wait is bounded.
+//   * split-K (grids with fewer tiles than SMs): the K-splits of one tile
+//     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 8).
+//     Each CTA parks its fp32 accumulator tile in its own shared memory (the
+//     drained stage ring), the cluster meets, and every CTA reduces a
+//     1/splits slice of the tile by reading all members' partials through
+//     distributed shared memory in rank order (deterministic), then stores
+//     it; a second cluster barrier keeps every CTA resident until its
+//     partial has been read.  No workspace, no atomics, no L2 round trip.
+// Per-CTA TMA loads only (no multicast); every mbarrier wait is bounded, and
+// every thread reaches both cluster barriers after its bounded waits.
 #pragma once
 
 #include "ql_common.cuh"
@@ -44,13 +53,14 @@ struct Params {
   long long lds, ldo;
   int M, N, K;
   int nk;                 // number of 128-k stages of K
-  int nk_split;           // stages per K-split (gridDim.z splits)
+  int nk_split;           // stages per K-split (gridDim.z splits = cluster size)
   int stages;             // shared-memory ring depth
   int scale_f32, bias_f32;
-  uint32_t* counters;     // [gridDim.y * gridDim.x] arrival counters (split-K)
-  float* partials;        // [gridDim.y * gridDim.x][gridDim.z][BN][128] fp32 (split-K)
   unsigned* err;
 };
+
+// Largest K-split (thread-block cluster size, portable limit).
+constexpr int kMaxSplits = 8;
 
 template <int WBITS, int BN>
 struct Layout {
@@ -62,7 +72,32 @@ struct Layout {
   static constexpr uint32_t kACol = BN <= 128 ? 128 : 256;  // first A column
   static constexpr uint32_t kTx = kStage;
   static size_t smem_bytes(int stages) { return 1024 + (size_t)stages * kStage + 256; }
+  // split-K: the fp32 partial [BN][128] is parked in the drained ring
+  static bool partial_fits(int stages) { return (size_t)BN * kTileN * 4 <= (size_t)stages * kStage; }
 };
+
+// ------------------------------------------------------ cluster helpers
+// Arrive (release) and wait (acquire) on the cluster barrier; not .aligned,
+// so the threads of a warp may arrive at different times.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Address of the same shared-memory offset in cluster member `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
 
 // ----------------------------------------------------------- tcgen05 ops
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
@@ -147,7 +182,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dfull = afree + kASlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);   // a wait of this CTA gave up
-  volatile int* last_flag = abort + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -370,63 +404,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
-      // Split-K: every CTA of the tile stores its fp32 partial [BN][128] in
-      // its own slot; the last to arrive sums the slots in split order,
-      // applies scale and bias, and zeroes its slots and the counter again.
-      const size_t tile_id = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
-      constexpr int kSlot = BN * kTileN;
-      float* slots = p.partials + tile_id * gridDim.z * kSlot;
-      float* mine = slots + (size_t)blockIdx.z * kSlot;
+      // Split-K: park the fp32 partial in this CTA's drained ring as
+      // [column m][row r] (consecutive rows -> consecutive banks).  Every
+      // TMA copy has landed and every MMA and decode read of the ring is
+      // done once dfull has fired.
+      float* part = reinterpret_cast<float*>(smem);
       #pragma unroll 1
       for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
         uint32_t v[8];
         tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
         #pragma unroll
-        for (int j = 0; j < 8; ++j) mine[(c0 + j) * kTileN + r] = __uint_as_float(v[j]);
-      }
-      named_bar_sync(1, 256);                       // the 8 epilogue warps
-      if (threadIdx.x == 64) {
-        // one thread releases the CTA's partials (cumulative over the
-        // barrier) and, if it arrives last, acquires the other splits'
-        __threadfence();
-        const unsigned old = atomicAdd(p.counters + tile_id, 1u);
-        const int last = old == gridDim.z - 1;
-        if (last) __threadfence();
-        *last_flag = last;
-      }
-      named_bar_sync(1, 256);
-      if (*last_flag) {
-        // 8 columns at a time: the 8 loads of a split are independent, so
-        // each split costs one L2 round trip per chunk (sums stay in split order)
-        #pragma unroll 1
-        for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          #pragma unroll 1
-          for (unsigned z = 0; z < gridDim.z; ++z) {
-            const float* sl = slots + (size_t)z * kSlot + (size_t)c0 * kTileN + r;
-            float t[8];
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) t[j] = __ldcg(sl + j * kTileN);
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] += t[j];
-          }
-          #pragma unroll 1
-          for (unsigned z = 0; z < gridDim.z; ++z) {   // leave the workspace zeroed
-            float* sl = slots + (size_t)z * kSlot + (size_t)c0 * kTileN + r;
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) __stcg(sl + j * kTileN, 0.f);
-          }
-          if (n < p.N) {
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int m = m0 + c0 + j;
-              if (m < p.M) p.out[(long long)m * p.ldo + n] = __float2half_rn(fmaf(acc[j], sc8, bv));
-            }
-          }
-        }
-        if (threadIdx.x == 64) p.counters[tile_id] = 0u;
+        for (int j = 0; j < 8; ++j) part[(c0 + j) * kTileN + r] = __uint_as_float(v[j]);
       }
     }
+  }
+
+  if (gridDim.z > 1) {
+    // ----------------------------------------------- cluster reduction
+    cluster_sync_all();                 // every member's partial is in its shared memory
+    if (warp >= 2) {
+      const int tid = (int)threadIdx.x - 64;
+      const int ks = (int)gridDim.z;
+      const uint32_t me = cluster_rank();
+      constexpr int E = BN * kTileN;
+      const int e0 = (int)(me * E / ks), e1 = (int)((me + 1) * E / ks);
+      const uint32_t base = smem_u32(smem);
+      uint32_t peer[kMaxSplits];
+      #pragma unroll
+      for (int q = 0; q < kMaxSplits; ++q) peer[q] = q < ks ? dsmem_addr(base, (uint32_t)q) : 0u;
+      // four elements per thread at a time: 4 x splits remote loads in flight
+      #pragma unroll 1
+      for (int eb = e0 + tid; eb < e1; eb += 4 * 256) {
+        float t[4][kMaxSplits];
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = eb + u * 256;
+          #pragma unroll
+          for (int q = 0; q < kMaxSplits; ++q)
+            t[u][q] = (q < ks && e < e1) ? ld_dsmem_f32(peer[q] + (uint32_t)e * 4u) : 0.f;
+        }
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = eb + u * 256;
+          float acc = 0.f;
+          #pragma unroll
+          for (int q = 0; q < kMaxSplits; ++q) acc += t[u][q];       // rank order; padding adds +0
+          const int nn = n0 + (e & (kTileN - 1));
+          const int m = m0 + (e >> 7);
+          if (e < e1 && nn < p.N && m < p.M) {
+            float s8 = 1.f, b = 0.f;
+            if (WBITS == 8)
+              s8 = p.scale_f32 ? static_cast<const float*>(p.scale)[nn]
+                               : __half2float(static_cast<const __half*>(p.scale)[nn]);
+            if (p.bias)
+              b = p.bias_f32 ? static_cast<const float*>(p.bias)[nn]
+                             : __half2float(static_cast<const __half*>(p.bias)[nn]);
+            p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc, s8, b));
+          }
+        }
+      }
+    }
+    cluster_sync_all();                 // no member leaves while its partial may still be read
   }
 
   tc_fence_before();

@@ -166,24 +166,42 @@ int make_gemm_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uin
 }
 
 // ------------------------------------------------------------- launch
+// cluster_z > 1: thread-block clusters of 1 x 1 x cluster_z CTAs.
 template <typename Kern, typename... Args>
-int launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+int launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, int cluster_z,
+              Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = (unsigned)cluster_z;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return QL_ERR_CUDA;
   }
   return QL_OK;
+}
+
+template <typename Kern, typename... Args>
+int launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+  return launch_ex(kernel, grid, block, smem, s, pdl, 1, args...);
 }
 
 // Raise the dynamic shared-memory limit of a kernel once per device.
@@ -512,16 +530,32 @@ int run_gemv(const LinearArgs& a, DeviceInfo* dev) {
 
 // ------------------------------------------------------------- GEMM plan
 // Activation rows per CTA (int4 tiles at 256 when the batch fills them:
-// three 72 KB stages fit; int8 stays at 128), and a K-split that brings a
-// grid of fewer tiles than SMs up to about one CTA per SM (at least two
-// stages per split).  Split-K needs workspace; without enough, no split.
+// three 72 KB stages fit; int8 stays at 128).  The K-split is chosen at
+// launch (launch_gemm_t): the splits of a tile are one thread-block cluster
+// and reduce through distributed shared memory, so no workspace is
+// involved.
 struct GemmPlan {
-  int bn = 0, ks = 1, nk_split = 0;
+  int bn = 0;
   int64_t tiles = 0;
-  size_t ws_bytes = 0, ws_counters = 0;
+  size_t ws_bytes = 0;   // always 0: K-splits reduce inside their cluster
 };
 
-GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail) {
+// Optional override for tuning sweeps: QLINEAR_GEMM_PLAN="ks,stages" (0 =
+// the planner's choice), read like QLINEAR_GEMV_PLAN.
+void gemm_override(int* ks, int* stages) {
+  static std::atomic<int> mode{-1};
+  int m = mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    m = std::getenv("QLINEAR_GEMM_PLAN") ? 1 : 0;
+    mode.store(m, std::memory_order_relaxed);
+  }
+  *ks = *stages = 0;
+  if (m == 0) return;
+  const char* e = std::getenv("QLINEAR_GEMM_PLAN");
+  if (e && std::sscanf(e, "%d,%d", ks, stages) != 2) *ks = *stages = 0;
+}
+
+GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan g;
   // int8 stages carry twice the weight bytes, so its widest tile is 192
   // rows (three 64 KB stages) where int4 takes 256 (three 72 KB stages);
@@ -529,50 +563,177 @@ GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t w
   // waves lose to the 128-row tile's 1.9)
   g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : wbits == 4 ? 256 : M >= 1024 ? 192 : 128;
   g.tiles = cdiv(N, ql::gemm::kTileN) * cdiv(M, g.bn);
-  const int64_t nk = K / 128;
-  int64_t ks = 1;
-  if (g.tiles < sms) ks = std::max<int64_t>(1, std::min<int64_t>(nk / 2, sms / g.tiles));
-  for (; ks > 1; --ks) {
-    const int64_t per = cdiv(nk, ks);
-    const int64_t eff = cdiv(nk, per);
-    const size_t counters = ((size_t)g.tiles * 4 + 255) / 256 * 256;
-    const size_t bytes = counters + (size_t)g.tiles * eff * g.bn * ql::gemm::kTileN * 4;
-    if (eff <= 65535 && bytes <= ws_avail) {
-      g.ks = (int)eff;
-      g.nk_split = (int)per;
-      g.ws_counters = counters;
-      g.ws_bytes = bytes;
-      return g;
-    }
-  }
-  g.ks = 1;
-  g.nk_split = (int)nk;
-  return g;
+  (void)K;
+  (void)sms;
+  return g;   // the K-split is chosen at launch, from the kernel's cluster occupancy
 }
 
+// How many clusters of cz CTAs of qgemm_kernel<WBITS, LAYOUT, BN> (with
+// `smem` dynamic bytes) fit on the device at once; 0 when the query fails.
+// Cached per instantiation, device and size (for the default ring depth).
 template <int WBITS, int LAYOUT, int BN>
-int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm,
-                  int ks) {
+int max_active_clusters(int cz, size_t smem, bool cacheable) {
+  auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
+  static std::atomic<int> cache[kMaxDevices][ql::gemm::kMaxSplits + 1];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cacheable && dev < kMaxDevices) {
+    const int c = cache[dev][cz].load(std::memory_order_relaxed);
+    if (c > 0) return c - 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, (unsigned)cz);
+  cfg.blockDim = dim3(ql::gemm::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)cz;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (cacheable && dev < kMaxDevices) cache[dev][cz].store(n + 1, std::memory_order_relaxed);
+  return n;
+}
+
+// CTAs of qgemm_kernel<WBITS, LAYOUT, BN> that share one SM, by shared
+// memory (whole carveout), registers and tensor memory.  The cluster
+// occupancy query above counts clusters as if one CTA held an SM (measured
+// on B200: 74 two-CTA clusters for 16- to 64-row tiles alike), while the
+// narrow tiles run two per SM; the launch plan scales by this.
+template <int WBITS, int LAYOUT, int BN>
+int ctas_per_sm(size_t smem) {
+  using L = ql::gemm::Layout<WBITS, BN>;
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < kMaxDevices) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int smem_sm = 0, reserved = 0;
+  cudaFuncAttributes fa;
+  if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>) != cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  int n = (int)((size_t)smem_sm / (smem + (size_t)reserved));
+  n = std::min(n, 65536 / std::max(1, fa.numRegs * ql::gemm::kThreads));
+  n = std::min(n, (int)(512 / L::kTmemCols));
+  n = std::max(1, n);
+  if (dev < kMaxDevices) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Ring depth and K-split of one tensor-core launch.  The split is the
+// largest cluster (at most kMaxSplits CTAs, at least two stages each) for
+// which a cluster per tile fits on the GPU at once: more splits shorten
+// each CTA's K loop, a second wave would double it.
+struct GemmLaunch {
+  int stages = 0, ks = 1, nk_split = 0, clusters_fit = 0;
+  size_t smem = 0;
+};
+
+template <int WBITS, int LAYOUT, int BN>
+int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
   using L = ql::gemm::Layout<WBITS, BN>;
   auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
   int S = (int)std::min<size_t>(6, (kSmemOptin - 1024 - 256) / L::kStage);
+  int o_ks, o_stages;
+  gemm_override(&o_ks, &o_stages);
+  if (o_stages > 0) S = std::min(S, o_stages);
   if (S < 3 && BN > 128) return QL_ERR_UNSUPPORTED;
   if (S < 2) return QL_ERR_UNSUPPORTED;
-  prm.stages = S;
   static std::atomic<unsigned char> done[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
   if (!done[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) != cudaSuccess) {
+    // the whole unified L1/shared array as shared memory, so that two CTAs
+    // of the narrow tiles share an SM (and the occupancy query knows it)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+            cudaSuccess) {
       cudaGetLastError();
       return QL_ERR_CUDA;
     }
     done[dev].store(1, std::memory_order_release);
   }
-  dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)ks);
+  g->stages = S;
+  g->smem = L::smem_bytes(S);
+  int ks = 1;
+  if (L::partial_fits(S)) {
+    if (o_ks > 0) {
+      ks = std::min(std::min(o_ks, ql::gemm::kMaxSplits), nk);
+    } else {
+      const int per_sm = o_stages <= 0 ? ctas_per_sm<WBITS, LAYOUT, BN>(g->smem) : 1;
+      for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
+        const int fit = max_active_clusters<WBITS, LAYOUT, BN>(c, g->smem, o_stages <= 0) * per_sm;
+        if (tiles <= fit) {
+          ks = c;
+          g->clusters_fit = fit;
+          break;
+        }
+      }
+    }
+  }
+  g->nk_split = (int)cdiv(nk, ks);
+  g->ks = (int)cdiv(nk, g->nk_split);
+  return QL_OK;
+}
+
+template <int WBITS, int LAYOUT, int BN>
+int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm,
+                  int64_t tiles) {
+  GemmLaunch g;
+  int st = gemm_launch_plan<WBITS, LAYOUT, BN>(tiles, prm.nk, &g);
+  if (st != QL_OK) return st;
+  prm.stages = g.stages;
+  prm.nk_split = g.nk_split;
+  dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)g.ks);
   if (grid.y > 65535 || grid.z > 65535) return QL_ERR_BAD_SHAPE;
-  return launch(kern, grid, dim3(ql::gemm::kThreads), L::smem_bytes(S), a.stream, (a.flags & QL_FLAG_PDL) != 0,
-                tx, tw, prm);
+  return launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem, a.stream,
+                   (a.flags & QL_FLAG_PDL) != 0, g.ks, tx, tw, prm);
+}
+
+// The launch plan of the tensor-core kernel for (wbits, layout, M, N, K).
+int gemm_plan_query(int wbits, int layout, int64_t M, int64_t N, int64_t K, int sms, GemmPlan* gp, GemmLaunch* gl) {
+  *gp = plan_gemm(wbits, M, N, K, sms);
+  const int nk = (int)(K / 128);
+  const int bn = gp->bn;
+#define QL_GEMM_PLAN_CASE(W, LY, B) return gemm_launch_plan<W, LY, B>(gp->tiles, nk, gl)
+  if (wbits == 8) {
+    switch (bn) {
+      case 16: QL_GEMM_PLAN_CASE(8, 0, 16);
+      case 32: QL_GEMM_PLAN_CASE(8, 0, 32);
+      case 64: QL_GEMM_PLAN_CASE(8, 0, 64);
+      case 128: QL_GEMM_PLAN_CASE(8, 0, 128);
+      default: QL_GEMM_PLAN_CASE(8, 0, 192);
+    }
+  }
+  if (layout == QL_W4_LAYOUT_SPLIT_HALF) {
+    switch (bn) {
+      case 16: QL_GEMM_PLAN_CASE(4, 0, 16);
+      case 32: QL_GEMM_PLAN_CASE(4, 0, 32);
+      case 64: QL_GEMM_PLAN_CASE(4, 0, 64);
+      case 128: QL_GEMM_PLAN_CASE(4, 0, 128);
+      default: QL_GEMM_PLAN_CASE(4, 0, 256);
+    }
+  }
+  switch (bn) {
+    case 16: QL_GEMM_PLAN_CASE(4, 1, 16);
+    case 32: QL_GEMM_PLAN_CASE(4, 1, 32);
+    case 64: QL_GEMM_PLAN_CASE(4, 1, 64);
+    case 128: QL_GEMM_PLAN_CASE(4, 1, 128);
+    default: QL_GEMM_PLAN_CASE(4, 1, 256);
+  }
+#undef QL_GEMM_PLAN_CASE
 }
 
 // Tensor-core path eligibility: int4 always (K % 128 == 0); int8 needs
@@ -601,39 +762,42 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.nk = (int)(a.K / 128);
-  p.nk_split = g.nk_split;
+  p.nk_split = p.nk;
   p.stages = 0;
   p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
   p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
-  p.counters = g.ks > 1 ? static_cast<uint32_t*>(a.ws) : nullptr;
-  p.partials = g.ks > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + g.ws_counters) : nullptr;
   p.err = dev->err_word;
   switch (bn) {
-    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.ks);
-    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.ks);
-    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.ks);
-    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.ks);
-    case 192: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.ks);
-    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.ks);
+    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.tiles);
+    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.tiles);
+    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.tiles);
+    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.tiles);
+    case 192: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles);
+    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles);
   }
 }
 
 int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
-  const GemmPlan g = plan_gemm(a.wbits, a.M, a.N, a.K, dev->sms, a.ws ? a.ws_bytes : 0);
+  const GemmPlan g = plan_gemm(a.wbits, a.M, a.N, a.K, dev->sms);
   if (a.wbits == 8) return run_gemm_layout<8, 0>(a, dev, g);
   if (a.layout == QL_W4_LAYOUT_SPLIT_HALF) return run_gemm_layout<4, 0>(a, dev, g);
   return run_gemm_layout<4, 1>(a, dev, g);
 }
 
-// Where the tensor-core GEMM replaces the decode kernel (measured on B200):
-// from 48 batch rows always (the decode kernel re-decodes the weights for
-// every 16-row batch chunk); from 16 on wide layers (lm_head, fused MLP
-// projections); for int8 from 24 rows when K is long.
-constexpr int64_t kGemmMinM = 48;
-constexpr int64_t kGemmMinMWide = 16;
-constexpr int64_t kWideN = 12288;
+// Where the tensor-core GEMM replaces the decode kernel (measured on B200
+// with the cluster split-K): from 24 batch rows always (the decode kernel
+// re-decodes the weights for every 16-row batch chunk); from 8 on small
+// layers (q/k/v/o-sized: the cluster split spreads them over every SM); from
+// 12 on tall-K layers and 7B-class lm_heads; from 16 on everything but
+// mid-width shallow layers (a small model's stacked gate+up, where the
+// decode kernel's fused SwiGLU epilogue keeps it ahead).
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
-  return M >= kGemmMinM || (M >= kGemmMinMWide && N >= kWideN) || (wbits == 8 && M >= 24 && K >= 4096);
+  (void)wbits;
+  if (M >= 24) return true;
+  if (M < 8) return false;
+  if ((double)N * (double)K <= 4.0e6) return true;
+  if (M >= 12 && (K >= 3 * N || (K >= 4096 && N >= 65536))) return true;
+  return M >= 16 && !(N >= 12288 && N < 32768 && K < 4096);
 }
 
 // Argument checks shared by the linear entry points; out_cols = the
@@ -898,7 +1062,7 @@ static size_t workspace_size(int wbits, int64_t M, int64_t N, int64_t K) {
   // enough for the kernel the dispatch picks; for the decode kernel, the
   // larger of its two int4 scale paths (a forced tensor-core call with less
   // workspace than its split-K needs simply runs unsplit)
-  if (K % 128 == 0 && use_gemm(wbits, M, N, K)) return plan_gemm(wbits, M, N, K, dev->sms, SIZE_MAX).ws_bytes;
+  if (K % 128 == 0 && use_gemm(wbits, M, N, K)) return plan_gemm(wbits, M, N, K, dev->sms).ws_bytes;
   size_t bytes = 0;
   for (int stma : {0, 1}) {
     GemvPlan pl;
@@ -935,6 +1099,25 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
   return QL_OK;
 }
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }
+
+int ql_gemm_plan(int wbits, int layout, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields) {
+  if (!fields || nfields < 8) return QL_ERR_NULL_POINTER;
+  if ((wbits != 4 && wbits != 8) || M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || M > 65535LL * 128 ||
+      N > INT_MAX)
+    return QL_ERR_BAD_SHAPE;
+  if (wbits == 4 && layout != QL_W4_LAYOUT_SPLIT_HALF && layout != QL_W4_LAYOUT_ADJACENT) return QL_ERR_UNSUPPORTED;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  GemmPlan gp;
+  GemmLaunch gl;
+  st = gemm_plan_query(wbits, layout, M, N, K, dev->sms, &gp, &gl);
+  if (st != QL_OK) return st;
+  const int64_t v[8] = {gp.bn, gl.ks, gl.nk_split, gl.stages, (int64_t)gl.smem, gp.tiles, gp.tiles * gl.ks,
+                        gl.clusters_fit};
+  for (int i = 0; i < 8; ++i) fields[i] = v[i];
+  return QL_OK;
+}
 
 int ql_w8a16_dequantize(const void* w_q, const void* scale, int scale_dtype, float* out, int64_t N, int64_t K,
                         int64_t ldw, void* stream) {

@@ -70,6 +70,7 @@ SIGNATURES = {
     "ql_w8a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_w4a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_gemv_plan": (_int, [_int, _i64, _i64, _i64, _sz, ctypes.POINTER(_i64), _int]),
+    "ql_gemm_plan": (_int, [_int, _int, _i64, _i64, _i64, ctypes.POINTER(_i64), _int]),
     "ql_w8a16_dequantize": (_int, [_vp, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "ql_w4a16_dequantize": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ql_w4a16_unpack": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
@@ -147,6 +148,17 @@ def gemv_plan(wbits: int, M: int, N: int, K: int, workspace_bytes: int | None = 
     avail = (1 << 64) - 1 if workspace_bytes is None else workspace_bytes
     check(load().ql_gemv_plan(wbits, M, N, K, avail, buf, 12))
     return dict(zip(PLAN_FIELDS, list(buf)))
+
+
+GEMM_PLAN_FIELDS = ("rows_per_tile", "k_splits", "stages_per_split", "ring_stages", "smem_bytes", "tiles",
+                    "ctas", "clusters_fit")
+
+
+def gemm_plan(wbits: int, M: int, N: int, K: int, layout: int = QL_W4_LAYOUT_SPLIT_HALF) -> dict:
+    """The tensor-core kernel's launch plan for a shape (see ql_gemm_plan)."""
+    buf = (_i64 * 8)()
+    check(load().ql_gemm_plan(wbits, layout, M, N, K, buf, 8))
+    return dict(zip(GEMM_PLAN_FIELDS, list(buf)))
 
 
 def version() -> tuple[int, int, int]:

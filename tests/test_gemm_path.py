@@ -116,8 +116,9 @@ def test_gemm_unsupported_shape_is_reported():
 @pytest.mark.parametrize("M", [1, 16, 33, 64, 200])
 @pytest.mark.parametrize("wbits", [4, 8])
 def test_gemm_split_k(K, N, M, wbits):
-    """Grids with fewer tiles than SMs split K across CTAs (workspace given):
-    parity, bit-identical repeat, workspace left zeroed."""
+    """Grids with fewer tiles than SMs split K across the CTAs of a cluster
+    (reduced through distributed shared memory): parity, bit-identical
+    repeat, a caller's workspace left untouched and none requested."""
     lin = make_linear(K, N, bias=True, std=0.02, seed=K + N + M + wbits)
     x = make_x(M, K, seed=M + 11)
     if wbits == 4:
@@ -133,7 +134,16 @@ def test_gemm_split_k(K, N, M, wbits):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert int(ws.count_nonzero()) == 0
+    c = _call(xd, qd, _lib.QL_FLAG_FORCE_GEMM)                     # no workspace: same plan, same bits
+    assert torch.equal(a, c)
     assert_parity(a, y32, x.numpy(), deq, f"split-K w{wbits} K{K} N{N} M{M}")
+
+
+def test_gemm_dispatch_needs_no_workspace():
+    lib = _lib.load()
+    for M, N, K in ((64, 8960, 1536), (64, 1536, 8960), (512, 4096, 14336), (16, 151936, 1536)):
+        assert lib.ql_w4a16_workspace_size(M, N, K) == 0
+        assert lib.ql_w8a16_workspace_size(M, N, K) == 0
 
 
 def test_gemm_no_device_error():
