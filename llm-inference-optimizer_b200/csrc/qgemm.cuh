@@ -25,7 +25,7 @@
 //     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
 //   * split-K (grids with fewer tiles than SMs): the K-splits of one tile
-//     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 8).
+//     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 16).
 //     Each CTA parks its fp32 accumulator tile in its own shared memory (the
 //     drained stage ring), the cluster meets, and every CTA reduces a
 //     1/splits slice of the tile by reading all members' partials through
@@ -59,8 +59,9 @@ struct Params {
   unsigned* err;
 };
 
-// Largest K-split (thread-block cluster size, portable limit).
-constexpr int kMaxSplits = 8;
+// Largest K-split = thread-block cluster size (beyond the portable 8: the
+// kernels are marked for non-portable cluster sizes, which B200 runs up to 16).
+constexpr int kMaxSplits = 16;
 
 template <int WBITS, int BN>
 struct Layout {
@@ -429,26 +430,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int E = BN * kTileN;
       const int e0 = (int)(me * E / ks), e1 = (int)((me + 1) * E / ks);
       const uint32_t base = smem_u32(smem);
-      uint32_t peer[kMaxSplits];
-      #pragma unroll
-      for (int q = 0; q < kMaxSplits; ++q) peer[q] = q < ks ? dsmem_addr(base, (uint32_t)q) : 0u;
-      // four elements per thread at a time: 4 x splits remote loads in flight
+      // four elements per thread at a time, up to 8 members per pass: up to
+      // 32 remote loads in flight; members are summed in rank order
       #pragma unroll 1
       for (int eb = e0 + tid; eb < e1; eb += 4 * 256) {
-        float t[4][kMaxSplits];
-        #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = eb + u * 256;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        #pragma unroll 1
+        for (int qb = 0; qb < ks; qb += 8) {
+          float t[4][8];
           #pragma unroll
-          for (int q = 0; q < kMaxSplits; ++q)
-            t[u][q] = (q < ks && e < e1) ? ld_dsmem_f32(peer[q] + (uint32_t)e * 4u) : 0.f;
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t peer = qb + q < ks ? dsmem_addr(base, (uint32_t)(qb + q)) : 0u;
+            #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int e = eb + u * 256;
+              t[u][q] = (qb + q < ks && e < e1) ? ld_dsmem_f32(peer + (uint32_t)e * 4u) : 0.f;
+            }
+          }
+          #pragma unroll
+          for (int u = 0; u < 4; ++u)
+            #pragma unroll
+            for (int q = 0; q < 8; ++q) acc[u] += t[u][q];              // padding adds +0
         }
         #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int e = eb + u * 256;
-          float acc = 0.f;
-          #pragma unroll
-          for (int q = 0; q < kMaxSplits; ++q) acc += t[u][q];       // rank order; padding adds +0
           const int nn = n0 + (e & (kTileN - 1));
           const int m = m0 + (e >> 7);
           if (e < e1 && nn < p.N && m < p.M) {
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.bias)
               b = p.bias_f32 ? static_cast<const float*>(p.bias)[nn]
                              : __half2float(static_cast<const __half*>(p.bias)[nn]);
-            p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc, s8, b));
+            p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc[u], s8, b));
           }
         }
       }
