@@ -262,6 +262,9 @@ void plan_override(int* tpc, int* ks) {
 // arithmetic is issue-bound at a fixed rate; the first data arrives after a
 // fixed latency; each block pays an epilogue and split-K a reduction.
 constexpr size_t kSmemShared = 110 * 1024;   // two CTAs per SM fit under this
+// Largest activation slice a CTA stages.  Measured: raising it to 176 KB
+// (8 rows of an 8960-wide K unsplit) made the planner pick slower plans.
+constexpr size_t kXStageMax = 96 * 1024;
 
 bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_avail, int scale_tma,
                GemvPlan* out, int64_t pair_n = 0) {
@@ -319,7 +322,7 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
       p.x_stride = kbps * epk + 8;
       p.x_rows = x_rows;
       p.wpt = std::min(kbps, ql::gemv::kMaxConsumerWarps / tpc);
-      if ((size_t)x_rows * p.x_stride * 2 > 96 * 1024) continue;
+      if ((size_t)x_rows * p.x_stride * 2 > kXStageMax) continue;
       p.ws_bytes = gemv_ws_bytes(p);
       if (p.ws_bytes > ws_avail) continue;
       const ql::gemv::Smem base =
