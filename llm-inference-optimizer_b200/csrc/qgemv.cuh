@@ -596,12 +596,10 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
       }
       named_bar_sync(1, nct);
       if (ctid == 0) {
-        // one thread releases the CTA's partials (the fence is cumulative over
-        // the barrier) and, if it arrives last, acquires the other splits'
-        __threadfence();
-        const unsigned old = atomicAdd(p.counters + tile_id, 1u);
+        // one thread releases the CTA's partials (cumulative over the
+        // barrier) and, if it arrives last, acquires the other splits'
+        const unsigned old = atomic_add_acq_rel_gpu(p.counters + tile_id, 1u);
         const int last = old == (unsigned)(p.ks - 1);
-        if (last) __threadfence();
         *last_flag = last;
       }
       named_bar_sync(1, nct);

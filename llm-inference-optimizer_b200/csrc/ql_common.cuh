@@ -82,6 +82,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// ------------------------------------------------------- arrival counters
+// Fetch-and-add with acquire-release semantics at GPU scope: the caller's
+// (and, through a preceding CTA barrier, its CTA's) writes are released
+// before the add, and the reads that follow see what the earlier arrivals
+// released.  One instruction instead of fence + atomic + fence.
+__device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");

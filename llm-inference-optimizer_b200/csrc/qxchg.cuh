@@ -120,10 +120,7 @@ __device__ __forceinline__ void publish_and_combine(const Ctx& c, int M, int tid
 __device__ __forceinline__ bool arrive_last(const Ctx& c, unsigned total) {
   const Layout L = layout(c.world, c.max_m);
   unsigned* counter = reinterpret_cast<unsigned*>(c.peer[c.rank] + L.state);
-  __threadfence();
-  const bool last = atomicAdd(counter, 1u) == total - 1;
-  if (last) __threadfence();
-  return last;
+  return atomic_add_acq_rel_gpu(counter, 1u) == total - 1;
 }
 
 __device__ __forceinline__ unsigned long long* scratch_of(const Ctx& c) {
