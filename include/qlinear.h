@@ -133,7 +133,8 @@ size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K);
  * per block, consumer warps per tile, K-splits, 128-byte k-blocks per split,
  * ring stages, batch tiles of 8 per CTA, batch chunks, CTAs launched (each
  * runs one or more blocks), dynamic shared bytes, workspace bytes, k-blocks
- * per stage, bytes of the innermost tensor-map dimension (nfields >= 12).  Has no
+ * per stage, bytes of the innermost tensor-map dimension (nfields >= 12), and
+ * with nfields >= 13 the planner's cost estimate in ns.  Has no
  * counterpart in the reference (its Triton configs are fixed in
  * _pick_config, w8a16_matmul_triton.py:89-99). */
 int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_bytes,

@@ -285,9 +285,9 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   // model constants (B200): HBM bandwidth, loaded latency, per-SM stream
   // cap, first-data latency, per-block epilogue, split-K reduction, and the
   // decode issue cost (warp instructions per 2 KB k-block of one tile)
-  const double bw_total = 6.5e12, lat = 2.0e-6, bw_sm_max = 120e9, t_fill = 1.5e-6, t_blk = 0.25e-6,
-               t_red = 4.0e-6, issue_rate = 2.5 * 1.9e9, bw_x_sm = 60e9;
-  const double ipk = (wbits == 4 ? 250.0 : 170.0) * (mt == 2 ? 1.3 : 1.0);
+  const double bw_total = 6.5e12, lat = 1.0e-6, bw_sm_max = 120e9, t_fill = 1.5e-6, t_blk = 0.25e-6,
+               t_red = 1.0e-6, t_red_blk = 0.5e-6, issue_rate = 2.5 * 1.9e9, bw_x_sm = 60e9;
+  const double ipk = (wbits == 4 ? 325.0 : 221.0) * (mt == 2 ? 1.3 : 1.0);
   int o_tpc, o_ks;
   plan_override(&o_tpc, &o_ks);
 
@@ -376,9 +376,12 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
         const double t_mem = bytes_cta / bw_cta + x_cta / bw_x_sm;
         const double tiles_kb = (double)NT * nkb * mchunks;   // 2 KB units, all CTAs
         const double t_comp = tiles_kb * ipk / (std::min<double>(ctas, sms) * issue_rate);
-        // split-K: a reduction at the end, and per block an arrival round trip
-        // that stalls the CTA's consumers (measured ~2 us per block)
-        q.cost = t_fill + std::max(t_mem, t_comp) + R * t_blk + (ks_eff > 1 ? t_red + R * 2.0e-6 : 0.0);
+        // The stream and the decode overlap only partly at these sizes (a CTA
+        // holds few stages): both terms count.  Split-K: a reduction at the
+        // end and per block an arrival round trip (one acquire-release
+        // atomic).  Constants fitted to forced-plan sweeps on B200 over the
+        // config-1/2 shapes at M = 1, 4, 8 and the 14336/4096 projections.
+        q.cost = t_fill + t_mem + t_comp + R * t_blk + (ks_eff > 1 ? t_red + R * t_red_blk : 0.0);
         // measured on B200: a warp should own 3..8 k-blocks of a tile's split
         // (fewer: the block epilogue dominates; more: the tile's stages drain
         // too slowly to keep its ring slots turning over)
@@ -1101,10 +1104,10 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
   const int sms = dev ? dev->sms : 148;   // without a device: the B200 SM count
   GemvPlan pl;
   if (!plan_gemv(wbits, M, N, K, sms, workspace_bytes, 1, &pl)) return QL_ERR_UNSUPPORTED;
-  const int64_t v[12] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
+  const int64_t v[13] = {pl.tpc, pl.wpt, pl.ks, pl.kbps, pl.stages, pl.mt, pl.mchunks,
                          (int64_t)pl.gx * pl.ks * pl.mchunks, (int64_t)pl.smem, (int64_t)pl.ws_bytes,
-                         pl.kb_stage, pl.chunk};
-  for (int i = 0; i < 12; ++i) fields[i] = v[i];
+                         pl.kb_stage, pl.chunk, (int64_t)(pl.cost * 1e9)};
+  for (int i = 0; i < std::min(nfields, 13); ++i) fields[i] = v[i];
   return QL_OK;
 }
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }

@@ -139,14 +139,14 @@ def check(status: int) -> None:
 
 PLAN_FIELDS = ("tiles_per_cta", "warps_per_tile", "k_splits", "kblocks_per_split", "stages",
                "batch_tiles", "batch_chunks", "ctas", "smem_bytes", "workspace_bytes", "kblocks_per_stage",
-               "chunk_bytes")
+               "chunk_bytes", "cost_ns")
 
 
 def gemv_plan(wbits: int, M: int, N: int, K: int, workspace_bytes: int | None = None) -> dict:
     """The decode-kernel plan for a shape (see ql_gemv_plan)."""
-    buf = (_i64 * 12)()
+    buf = (_i64 * 13)()
     avail = (1 << 64) - 1 if workspace_bytes is None else workspace_bytes
-    check(load().ql_gemv_plan(wbits, M, N, K, avail, buf, 12))
+    check(load().ql_gemv_plan(wbits, M, N, K, avail, buf, 13))
     return dict(zip(PLAN_FIELDS, list(buf)))
 
 
