@@ -397,7 +397,8 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
                          "frac": per_rank_gbs / peak, "peak_kind": peak_kind,
-                         "kernel": "qgemv_kernel<4,0,*> (W4A16 decode GEMV)",
+                         "kernel": "qgemv_kernel<4,0,*> (M 1, 8) and qgemm_kernel<4,0,32> (M 32): the "
+                                   "step's 216 launches averaged",
                          "bytes_per_launch": avg_launch_bytes,
                          "traffic": traffic, "pct_of_8TBs": per_rank_gbs / 8000.0},
             "cpu_baseline": cpu_baseline,
