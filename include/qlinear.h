@@ -89,11 +89,13 @@ extern "C" {
  *   scale    [N], scale_dtype QL_DTYPE_F32 (reference) or QL_DTYPE_F16
  *   bias     [N] or NULL, bias_dtype QL_DTYPE_F16 or QL_DTYPE_F32
  *   out      fp16 [M, ldo]
- *   workspace / workspace_bytes: optional scratch for split-K.  Must be
- *     zero-filled before its first use; every call leaves it zero-filled.
- *     With NULL (or too small) the kernel is planned without split-K, which
- *     is always valid but can be slower for tall-K shapes.  Calls that share
- *     one workspace must not run concurrently (use one per stream).
+ *   workspace / workspace_bytes: optional scratch for the decode kernel's
+ *     split-K (the tensor-core kernel reduces its K-splits inside a
+ *     thread-block cluster and needs none).  Must be zero-filled before its
+ *     first use; every call leaves it zero-filled.  With NULL (or too small)
+ *     the decode kernel is planned without split-K, which is always valid
+ *     but can be slower for tall-K shapes.  Calls that share one workspace
+ *     must not run concurrently (use one per stream).
  */
 int ql_w8a16_linear(const void* x, int x_dtype,
                     const void* w_q,
