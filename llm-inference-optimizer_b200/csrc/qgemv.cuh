@@ -410,6 +410,8 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   if (WBITS == 4 && !scale_tma) stage_scales(blockIdx.x);
 
   griddep_wait();   // x (and out / workspace) may belong to the previous kernel
+  // greedy head: the exchange's epoch, read now rather than in the tail
+  const unsigned xchg_done = (greedy && ctid == 0) ? xchg::epochs_done(p.amax) : 0u;
 
   const int mvalid = min(MC, p.M - m0);
   // x slice [m0, m0+mvalid) x [kx0, kx0 + kbc*EPK) -> shared memory, once per
@@ -634,9 +636,14 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
     unsigned long long* scratch = xchg::scratch_of(p.amax);
     for (int i = ctid; i < mvalid; i += nct) atomicMax(scratch + m0 + i, amax_s[i]);
     named_bar_sync(1, nct);
-    if (ctid == 0) *last_flag = xchg::arrive_last(p.amax, gridDim.x * gridDim.y * gridDim.z) ? 1 : 0;
+    if (ctid == 0) {
+      *last_flag = xchg::arrive_last(p.amax, gridDim.x * gridDim.y * gridDim.z) ? 1 : 0;
+      amax_s[0] = xchg_done;            // hand the epoch to the other threads (row maxima are merged)
+    }
     named_bar_sync(1, nct);
-    if (*last_flag) xchg::publish_and_combine(p.amax, p.M, ctid, nct, p.err, [&] { named_bar_sync(1, nct); });
+    if (*last_flag)
+      xchg::publish_and_combine(p.amax, p.M, ctid, nct, p.err, [&] { named_bar_sync(1, nct); },
+                                (unsigned)amax_s[0]);
   }
 }
 

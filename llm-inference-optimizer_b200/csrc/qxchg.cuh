@@ -67,19 +67,41 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned 
 }
 constexpr unsigned long long kKeyMask = 0xFFFFFFFFFFFFull;   // the 48 key bits
 
+// Calls completed so far on this rank's buffer (read once the kernel
+// before has finished: only the last CTA of a call changes it, at its end).
+__device__ __forceinline__ unsigned epochs_done(const Ctx& c) {
+  const Layout L = layout(c.world, c.max_m);
+  return *reinterpret_cast<const volatile unsigned*>(c.peer[c.rank] + L.state + 4);
+}
+
 // This rank's row maxima (scratch) are complete: push them, tagged with the
 // call's epoch, into every rank's bank, wait (bounded) for every rank's,
 // write the argmax columns and reset scratch, the CTA counter and the epoch
-// for the next call.  Run by all `nthr` threads of the last CTA; `bar`
-// synchronises them.
+// for the next call (one rank: the columns straight from scratch).  Run by
+// all `nthr` threads of the last CTA; `bar` synchronises them; `done` =
+// epochs_done() read earlier in the kernel.
 template <class Bar>
-__device__ __forceinline__ void publish_and_combine(const Ctx& c, int M, int tid, int nthr, unsigned* err, Bar bar) {
+__device__ __forceinline__ void publish_and_combine(const Ctx& c, int M, int tid, int nthr, unsigned* err, Bar bar,
+                                                    unsigned done) {
   const Layout L = layout(c.world, c.max_m);
   unsigned char* own = c.peer[c.rank];
   unsigned long long* scratch = reinterpret_cast<unsigned long long*>(own + L.scratch);
   unsigned* counter = reinterpret_cast<unsigned*>(own + L.state);
   unsigned* epoch_done = counter + 1;
-  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch_done) + 1u;
+  const unsigned e = done + 1u;
+  if (c.world == 1) {
+    for (int i = tid; i < M; i += nthr) {
+      const unsigned long long b = ld_volatile_u64(scratch + i) & kKeyMask;
+      c.out[i] = (long long)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull));
+      scratch[i] = 0ull;
+    }
+    bar();
+    if (tid == 0) {
+      *counter = 0u;
+      *reinterpret_cast<volatile unsigned*>(epoch_done) = e;
+    }
+    return;
+  }
   const int bank = (int)(e & 1u);
   const unsigned long long tag = (unsigned long long)((e & 0x7FFFu) | 0x8000u) << 48;   // never 0
   for (int q = 0; q < c.world; ++q) {
@@ -131,10 +153,12 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
   unsigned long long* scratch = scratch_of(p.c);
   __shared__ unsigned long long red[8];
   __shared__ int is_last;
+  __shared__ unsigned done_s;
 
   // the logits come from the kernel before (launched with programmatic
   // dependent launch, this kernel is resident early and waits here)
   griddep_wait();
+  const unsigned done = threadIdx.x == 0 ? epochs_done(p.c) : 0u;   // off the tail's critical path
 
   // ---- local reduction of this CTA's chunk of row m
   const int m = blockIdx.y;
@@ -164,12 +188,13 @@ __global__ void __launch_bounds__(256) argmax_exchange_kernel(const Params p) {
     for (int w = 1; w < 8; ++w) b = amax::umax64(b, red[w]);
     atomicMax(scratch + m, b);
     is_last = arrive_last(p.c, gridDim.x * gridDim.y);
+    done_s = done;
   }
   __syncthreads();
   if (!is_last) return;
 
   // ---- last CTA: push tagged keys, wait for every rank's, combine
-  publish_and_combine(p.c, p.M, (int)threadIdx.x, (int)blockDim.x, p.err, [] { __syncthreads(); });
+  publish_and_combine(p.c, p.M, (int)threadIdx.x, (int)blockDim.x, p.err, [] { __syncthreads(); }, done_s);
 }
 
 }  // namespace xchg
