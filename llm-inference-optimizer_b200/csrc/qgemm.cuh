@@ -8,7 +8,8 @@
 // "Swap-AB" formulation: D[n, m] = sum_k W[n, k] * x[m, k], so the
 // dequantized weights are the MMA's A operand (M = 128 weight rows per CTA)
 // and the activations are the B operand (N = BN activation rows per CTA).
-//   * warp 0 (one thread): TMA producer.  Per 128-k stage it loads the
+//   * warp 0 (one thread): TMA producer (the first ring-full of weight
+//     stages is issued before waiting for the kernel before).  Per 128-k stage it loads the
 //     packed weight tile (128 rows x 64 B int4 / 128 B int8, 64/128-byte
 //     swizzle, a 3-D view of the rows) and the activation tile (BN rows x
 //     128 k as two 128-byte-swizzled K-major atoms).
@@ -220,17 +221,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_w);
       const uint64_t pol_w = l2_policy_evict_last();   // reused by every activation tile
       const uint64_t pol_x = l2_policy_evict_last();   // reused by every weight tile
+      // The weights of the first ring-full of stages do not depend on the
+      // kernel before (programmatic dependent launch): they stream while it
+      // finishes; the activations follow once it has.
+      const int pre = min(S, nk);
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* st = smem + (size_t)i * L::kStage;
+        mbar_arrive_expect_tx(full + i, L::kTx);
+        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, full + i, pol_w);
+      }
       griddep_wait();
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* st = smem + (size_t)i * L::kStage;
+        tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, full + i, pol_x);
+        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, full + i, pol_x);
+      }
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
         const int s = i % S;
-        if (i >= S) {
-          const uint32_t par = ((i / S) - 1) & 1;
-          if (!mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait, abort) ||
-              !mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort)) {
-            *abort = 1;
-            break;
-          }
+        const uint32_t par = ((i / S) - 1) & 1;
+        if (!mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait, abort) ||
+            !mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort)) {
+          *abort = 1;
+          break;
         }
         uint8_t* st = smem + (size_t)s * L::kStage;
         mbar_arrive_expect_tx(full + s, L::kTx);
