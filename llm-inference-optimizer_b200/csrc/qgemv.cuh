@@ -418,16 +418,50 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
   // CTA (every block of the CTA uses the same slice); k past K reads as
   // zero.  Rows >= mvalid are never read.
   {
+    // Up to 8 16-byte loads in flight per thread before any is stored (one
+    // after another they would be serial L2 round trips on the critical
+    // path): 8 of a thread's vectors of a single row, or one vector of up
+    // to 8 rows.
     const int kx0 = kb0 * EPK;
     const int nvec = kbc * EPK / 8;
-    for (int mr = 0; mr < mvalid; ++mr) {
-      const __half* xrow = p.x + (long long)(m0 + mr) * p.ldx + kx0;
-      __half* srow = xs + mr * p.x_stride;
-      for (int v = ctid; v < nvec; v += nct) {
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (kx0 + v * 8 < p.K) val = ldg_cg_v4(xrow + v * 8);
-        if (WBITS == 4) val = stage_x_perm<LAYOUT>(val);   // k order of the permuted int4 decode
-        *reinterpret_cast<uint4*>(srow + v * 8) = val;
+    if (mvalid == 1) {
+      const __half* xrow = p.x + (long long)m0 * p.ldx + kx0;
+      for (int v0 = ctid; v0 < nvec; v0 += 8 * nct) {
+        uint4 val[8];
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + u * nct;
+          val[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (v < nvec && kx0 + v * 8 < p.K) val[u] = ldg_cg_v4(xrow + v * 8);
+        }
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int v = v0 + u * nct;
+          if (v < nvec) {
+            uint4 w = val[u];
+            if (WBITS == 4) w = stage_x_perm<LAYOUT>(w);   // k order of the permuted int4 decode
+            *reinterpret_cast<uint4*>(xs + v * 8) = w;
+          }
+        }
+      }
+    } else for (int v = ctid; v < nvec; v += nct) {
+      const bool in_k = kx0 + v * 8 < p.K;
+      #pragma unroll
+      for (int r0 = 0; r0 < MC; r0 += 8) {
+        uint4 val[8];
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          val[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (r0 + u < mvalid && in_k) val[u] = ldg_cg_v4(p.x + (long long)(m0 + r0 + u) * p.ldx + kx0 + v * 8);
+        }
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (r0 + u < mvalid) {
+            uint4 w = val[u];
+            if (WBITS == 4) w = stage_x_perm<LAYOUT>(w);   // k order of the permuted int4 decode
+            *reinterpret_cast<uint4*>(xs + (r0 + u) * p.x_stride + v * 8) = w;
+          }
+        }
       }
     }
     if (greedy)
