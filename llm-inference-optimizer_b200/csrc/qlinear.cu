@@ -286,7 +286,7 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
   // cap, first-data latency, per-block epilogue, split-K reduction, and the
   // decode issue cost (warp instructions per 2 KB k-block of one tile)
   const double bw_total = 6.5e12, lat = 1.0e-6, bw_sm_max = 120e9, t_fill = 1.5e-6, t_blk = 0.25e-6,
-               t_red = 1.0e-6, t_red_blk = 0.5e-6, issue_rate = 2.5 * 1.9e9, bw_x_sm = 60e9;
+               t_red = 1.0e-6, t_red_blk = 0.5e-6, issue_rate = 2.5 * 1.9e9, bw_x_sm = 480e9;
   const double ipk = (wbits == 4 ? 325.0 : 221.0) * (mt == 2 ? 1.3 : 1.0);
   int o_tpc, o_ks;
   plan_override(&o_tpc, &o_ks);
@@ -380,7 +380,8 @@ bool plan_gemv(int wbits, int64_t M, int64_t N, int64_t K, int sms, size_t ws_av
         // holds few stages): both terms count.  Split-K: a reduction at the
         // end and per block an arrival round trip (one acquire-release
         // atomic).  Constants fitted to forced-plan sweeps on B200 over the
-        // config-1/2 shapes at M = 1, 4, 8 and the 14336/4096 projections.
+        // config-1/2 shapes at M = 1, 4, 8 and the 14336/4096 projections
+        // (the x slice is staged with 8 loads in flight per thread: fast).
         q.cost = t_fill + t_mem + t_comp + R * t_blk + (ks_eff > 1 ? t_red + R * t_red_blk : 0.0);
         // measured on B200: a warp should own 3..8 k-blocks of a tile's split
         // (fewer: the block epilogue dominates; more: the tile's stages drain
