@@ -797,20 +797,20 @@ int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
   return run_gemm_layout<4, 1>(a, dev, g);
 }
 
-// Where the tensor-core GEMM replaces the decode kernel (measured on B200
-// with the cluster split-K): from 24 batch rows always (the decode kernel
-// re-decodes the weights for every 16-row batch chunk); from 8 on small
-// layers (q/k/v/o-sized: the cluster split spreads them over every SM); from
-// 12 on tall-K layers and 7B-class lm_heads; from 16 on everything but
-// mid-width shallow layers (a small model's stacked gate+up, where the
-// decode kernel's fused SwiGLU epilogue keeps it ahead).
+// Where the tensor-core GEMM replaces the decode kernel (measured on B200:
+// forced-path sweeps of both over M = 8..32 on the config-1 to 4 shapes):
+// from 24 batch rows always (the decode kernel re-decodes the weights for
+// every 16-row batch chunk); below that only where the decode kernel would
+// need a K-split through the workspace — tall-K layers (K >= 3N) from 12
+// rows (from 8 when K >= 12288), and layers with K >= 4096 wider than 12288
+// (up/gate of 7B-class models, their lm_heads) from 12.  Small (q/k/v/o)
+// and shallow wide layers stay on the decode kernel up to 23 rows.
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
   (void)wbits;
   if (M >= 24) return true;
   if (M < 8) return false;
-  if ((double)N * (double)K <= 4.0e6) return true;
-  if (M >= 12 && (K >= 3 * N || (K >= 4096 && N >= 65536))) return true;
-  return M >= 16 && !(N >= 12288 && N < 32768 && K < 4096);
+  if (K >= 3 * N && (M >= 12 || K >= 12288)) return true;
+  return M >= 12 && K >= 4096 && N >= 12288;
 }
 
 // Argument checks shared by the linear entry points; out_cols = the

@@ -141,7 +141,7 @@ def test_gemm_split_k(K, N, M, wbits):
 
 def test_gemm_dispatch_needs_no_workspace():
     lib = _lib.load()
-    for M, N, K in ((64, 8960, 1536), (64, 1536, 8960), (512, 4096, 14336), (16, 151936, 1536)):
+    for M, N, K in ((64, 8960, 1536), (64, 1536, 8960), (512, 4096, 14336), (32, 151936, 1536), (16, 1536, 8960)):
         assert lib.ql_w4a16_workspace_size(M, N, K) == 0
         assert lib.ql_w8a16_workspace_size(M, N, K) == 0
 
