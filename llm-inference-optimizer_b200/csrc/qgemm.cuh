@@ -168,6 +168,48 @@ __device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
+// Sums elements [e0, e1) of the tile's partial ([column m][row r] fp32 in
+// every member's shared memory at `base`) over the ks members in rank order
+// and stores them with scale and bias.  EB elements per thread per batch,
+// all of up to KS members' values in flight together.
+template <int WBITS, int EB, int KS>
+__device__ __forceinline__ void reduce_slice(const Params& p, uint32_t base, int ks, int e0, int e1, int tid,
+                                             int n0, int m0) {
+  constexpr int kStride = 256;   // the 8 epilogue warps
+  #pragma unroll 1
+  for (int eb = e0 + tid; eb < e1; eb += EB * kStride) {
+    float t[EB][KS];
+    #pragma unroll
+    for (int q = 0; q < KS; ++q) {
+      const uint32_t peer = q < ks ? dsmem_addr(base, (uint32_t)q) : 0u;
+      #pragma unroll
+      for (int u = 0; u < EB; ++u) {
+        const int e = eb + u * kStride;
+        t[u][q] = (q < ks && e < e1) ? ld_dsmem_f32(peer + (uint32_t)e * 4u) : 0.f;
+      }
+    }
+    #pragma unroll
+    for (int u = 0; u < EB; ++u) {
+      const int e = eb + u * kStride;
+      float acc = 0.f;
+      #pragma unroll
+      for (int q = 0; q < KS; ++q) acc += t[u][q];                 // rank order; padding adds +0
+      const int nn = n0 + (e & (kTileN - 1));
+      const int m = m0 + (e >> 7);
+      if (e < e1 && nn < p.N && m < p.M) {
+        float s8 = 1.f, b = 0.f;
+        if (WBITS == 8)
+          s8 = p.scale_f32 ? static_cast<const float*>(p.scale)[nn]
+                           : __half2float(static_cast<const __half*>(p.scale)[nn]);
+        if (p.bias)
+          b = p.bias_f32 ? static_cast<const float*>(p.bias)[nn]
+                         : __half2float(static_cast<const __half*>(p.bias)[nn]);
+        p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc, s8, b));
+      }
+    }
+  }
+}
+
 template <int WBITS, int LAYOUT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -437,51 +479,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------- cluster reduction
     cluster_sync_all();                 // every member's partial is in its shared memory
     if (warp >= 2) {
-      const int tid = (int)threadIdx.x - 64;
       const int ks = (int)gridDim.z;
       const uint32_t me = cluster_rank();
       constexpr int E = BN * kTileN;
       const int e0 = (int)(me * E / ks), e1 = (int)((me + 1) * E / ks);
-      const uint32_t base = smem_u32(smem);
-      // four elements per thread at a time, up to 8 members per pass: up to
-      // 32 remote loads in flight; members are summed in rank order
-      #pragma unroll 1
-      for (int eb = e0 + tid; eb < e1; eb += 4 * 256) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        #pragma unroll 1
-        for (int qb = 0; qb < ks; qb += 8) {
-          float t[4][8];
-          #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint32_t peer = qb + q < ks ? dsmem_addr(base, (uint32_t)(qb + q)) : 0u;
-            #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int e = eb + u * 256;
-              t[u][q] = (qb + q < ks && e < e1) ? ld_dsmem_f32(peer + (uint32_t)e * 4u) : 0.f;
-            }
-          }
-          #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[u] += t[u][q];              // padding adds +0
-        }
-        #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = eb + u * 256;
-          const int nn = n0 + (e & (kTileN - 1));
-          const int m = m0 + (e >> 7);
-          if (e < e1 && nn < p.N && m < p.M) {
-            float s8 = 1.f, b = 0.f;
-            if (WBITS == 8)
-              s8 = p.scale_f32 ? static_cast<const float*>(p.scale)[nn]
-                               : __half2float(static_cast<const __half*>(p.scale)[nn]);
-            if (p.bias)
-              b = p.bias_f32 ? static_cast<const float*>(p.bias)[nn]
-                             : __half2float(static_cast<const __half*>(p.bias)[nn]);
-            p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc[u], s8, b));
-          }
-        }
-      }
+      // all members' values of a batch of elements are loaded before any is
+      // summed (one remote round trip per batch): 8 elements x up to 4
+      // members, or 2 elements x up to 16 (32 registers, so that the narrow
+      // tiles still run two CTAs per SM)
+      if (ks <= 4)
+        reduce_slice<WBITS, 8, 4>(p, smem_u32(smem), ks, e0, e1, (int)threadIdx.x - 64, n0, m0);
+      else
+        reduce_slice<WBITS, 2, kMaxSplits>(p, smem_u32(smem), ks, e0, e1, (int)threadIdx.x - 64, n0, m0);
     }
     cluster_sync_all();                 // no member leaves while its partial may still be read
   }
