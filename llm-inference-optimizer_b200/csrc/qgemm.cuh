@@ -73,9 +73,18 @@ struct Layout {
   static constexpr uint32_t kTmemCols = BN + kASlots * 64 <= 256 ? 256 : 512;
   static constexpr uint32_t kACol = BN <= 128 ? 128 : 256;  // first A column
   static constexpr uint32_t kTx = kStage;
-  static size_t smem_bytes(int stages) { return 1024 + (size_t)stages * kStage + 256; }
-  // split-K: the fp32 partial [BN][128] is parked in the drained ring
-  static bool partial_fits(int stages) { return (size_t)BN * kTileN * 4 <= (size_t)stages * kStage; }
+  // Split-K reduction: narrow tiles push their partial into the members'
+  // receive buffers (one cluster barrier); wide tiles park it in the
+  // drained ring and the members pull (two barriers, no extra memory).
+  static constexpr bool kPush = BN <= 32;   // measured: 64-row tiles pull faster
+  // receive buffer [splits][ceil(BN*128/splits)] fp32 (push mode)
+  static constexpr size_t kRecvBytes = (((size_t)BN * kTileN + kMaxSplits) * 4 + 1023) / 1024 * 1024;
+  __host__ __device__ static constexpr size_t kRecvOffset(int stages) { return (size_t)stages * kStage + 256; }
+  static size_t smem_bytes(int stages, bool split = false) {
+    return 1024 + (size_t)stages * kStage + 256 + (split && kPush ? kRecvBytes : 0);
+  }
+  // pull mode: the fp32 partial [BN][128] is parked in the drained ring
+  static bool partial_fits(int stages) { return kPush || (size_t)BN * kTileN * 4 <= (size_t)stages * kStage; }
 };
 
 // ------------------------------------------------------ cluster helpers
@@ -94,6 +103,9 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -459,8 +471,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+    } else if (L::kPush) {
+      // Split-K, push: element e = m*128 + r of the partial belongs to
+      // member e / sz, which sums it; store it straight into that member's
+      // receive buffer, slot of this CTA's rank (remote stores, no reply)
+      const int ks = (int)gridDim.z;
+      const int sz = (BN * kTileN + ks - 1) / ks;
+      const uint32_t me = cluster_rank();
+      const uint32_t recv = smem_u32(smem + L::kRecvOffset(S));
+      int e = half * kHalfCols * kTileN + r;
+      int owner = e / sz, off = e - owner * sz;
+      #pragma unroll 1
+      for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+        uint32_t v[8];
+        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_dsmem_f32(dsmem_addr(recv + (uint32_t)(me * sz + off) * 4u, (uint32_t)owner), __uint_as_float(v[j]));
+          off += kTileN;                     // next column, same row
+          while (off >= sz) {
+            off -= sz;
+            ++owner;
+          }
+        }
+      }
     } else {
-      // Split-K: park the fp32 partial in this CTA's drained ring as
+      // Split-K, pull: park the fp32 partial in this CTA's drained ring as
       // [column m][row r] (consecutive rows -> consecutive banks).  Every
       // TMA copy has landed and every MMA and decode read of the ring is
       // done once dfull has fired.
@@ -475,8 +511,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (gridDim.z > 1) {
-    // ----------------------------------------------- cluster reduction
+  if (gridDim.z > 1 && L::kPush) {
+    // ------------------------------------------ cluster reduction (push)
+    cluster_sync_all();                 // every member's slices are in this CTA's receive buffer
+    if (warp >= 2) {
+      const int ks = (int)gridDim.z;
+      constexpr int E = BN * kTileN;
+      const int sz = (E + ks - 1) / ks;
+      const uint32_t me = cluster_rank();
+      const int e0 = (int)me * sz, e1 = min(E, e0 + sz);
+      const float* recv = reinterpret_cast<const float*>(smem + L::kRecvOffset(S));
+      for (int e = e0 + (int)threadIdx.x - 64; e < e1; e += 256) {
+        float acc = 0.f;
+        for (int q = 0; q < ks; ++q) acc += recv[q * sz + (e - e0)];   // rank order
+        const int nn = n0 + (e & (kTileN - 1));
+        const int m = m0 + (e >> 7);
+        if (nn < p.N && m < p.M) {
+          float s8 = 1.f, b = 0.f;
+          if (WBITS == 8)
+            s8 = p.scale_f32 ? static_cast<const float*>(p.scale)[nn]
+                             : __half2float(static_cast<const __half*>(p.scale)[nn]);
+          if (p.bias)
+            b = p.bias_f32 ? static_cast<const float*>(p.bias)[nn]
+                           : __half2float(static_cast<const __half*>(p.bias)[nn]);
+          p.out[(long long)m * p.ldo + nn] = __float2half_rn(fmaf(acc, s8, b));
+        }
+      }
+    }
+    // nothing touches this CTA's shared memory after the barrier: no second one
+  } else if (gridDim.z > 1) {
+    // ------------------------------------------ cluster reduction (pull)
     cluster_sync_all();                 // every member's partial is in its shared memory
     if (warp >= 2) {
       const int ks = (int)gridDim.z;

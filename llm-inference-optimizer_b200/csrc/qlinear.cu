@@ -262,6 +262,9 @@ void plan_override(int* tpc, int* ks) {
 // arithmetic is issue-bound at a fixed rate; the first data arrives after a
 // fixed latency; each block pays an epilogue and split-K a reduction.
 constexpr size_t kSmemShared = 110 * 1024;   // two CTAs per SM fit under this
+// dynamic shared memory at which two CTAs still share an SM (228 KB per SM,
+// 1 KB reserved per CTA)
+constexpr size_t kSmemTwoPerSm = 233472 / 2 - 1024;
 // Largest activation slice a CTA stages.  Measured: raising it to 176 KB
 // (8 rows of an 8960-wide K unsplit) made the planner pick slower plans.
 constexpr size_t kXStageMax = 96 * 1024;
@@ -673,10 +676,16 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
     }
     done[dev].store(1, std::memory_order_release);
   }
-  g->stages = S;
-  g->smem = L::smem_bytes(S);
+  // split launches (push mode) carry a receive buffer; the narrow tiles
+  // give up ring stages rather than the second CTA on the SM
+  int S_split = S;
+  while (S_split > 2 && L::smem_bytes(S_split, true) > kSmemOptin) --S_split;
+  if (BN <= 32)
+    while (S_split > 2 && L::smem_bytes(S_split, true) > kSmemTwoPerSm) --S_split;
+  g->stages = S_split;
+  g->smem = L::smem_bytes(S_split, true);
   int ks = 1;
-  if (L::partial_fits(S)) {
+  if (L::smem_bytes(S_split, true) <= kSmemOptin && L::partial_fits(S_split)) {
     if (o_ks > 0) {
       ks = std::min(std::min(o_ks, ql::gemm::kMaxSplits), nk);
     } else {
@@ -698,6 +707,10 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
   }
   g->nk_split = (int)cdiv(nk, ks);
   g->ks = (int)cdiv(nk, g->nk_split);
+  if (g->ks == 1) {
+    g->stages = S;
+    g->smem = L::smem_bytes(S);
+  }
   return QL_OK;
 }
 
