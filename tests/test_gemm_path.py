@@ -113,12 +113,14 @@ def test_gemm_unsupported_shape_is_reported():
 
 
 @pytest.mark.parametrize("K,N", [(8960, 1536), (1536, 8960), (4096, 256), (2048, 1000)])
-@pytest.mark.parametrize("M", [1, 16, 33, 64, 200])
+@pytest.mark.parametrize("M", [1, 16, 32, 33, 64, 200])
 @pytest.mark.parametrize("wbits", [4, 8])
 def test_gemm_split_k(K, N, M, wbits):
     """Grids with fewer tiles than SMs split K across the CTAs of a cluster
-    (reduced through distributed shared memory): parity, bit-identical
-    repeat, a caller's workspace left untouched and none requested."""
+    (reduced through distributed shared memory: pushed into the summing
+    member for 16/32-row tiles, pulled for wider ones): parity,
+    bit-identical repeat, a caller's workspace left untouched and none
+    requested."""
     lin = make_linear(K, N, bias=True, std=0.02, seed=K + N + M + wbits)
     x = make_x(M, K, seed=M + 11)
     if wbits == 4:
