@@ -26,15 +26,18 @@
 //     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
 //   * split-K (grids with fewer tiles than SMs): the K-splits of one tile
-//     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 16).
-//     Each CTA parks its fp32 accumulator tile in its own shared memory (the
-//     drained stage ring), the cluster meets, and every CTA reduces a
-//     1/splits slice of the tile by reading all members' partials through
-//     distributed shared memory in rank order (deterministic), then stores
-//     it; a second cluster barrier keeps every CTA resident until its
-//     partial has been read.  No workspace, no atomics, no L2 round trip.
+//     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 16);
+//     every member sums a 1/splits slice of the tile in rank order
+//     (deterministic) and stores it.  Narrow activation tiles (16/32 rows)
+//     push: each CTA stores its partial's elements straight into the
+//     receive buffer of the member that sums them, and one cluster barrier
+//     publishes them.  Wider tiles pull: each CTA parks its partial in its
+//     drained stage ring, the cluster meets, the members read the slices
+//     they sum through distributed shared memory, and a second barrier keeps
+//     every CTA resident until its partial has been read.  No workspace, no
+//     atomics, no L2 round trip.
 // Per-CTA TMA loads only (no multicast); every mbarrier wait is bounded, and
-// every thread reaches both cluster barriers after its bounded waits.
+// every thread reaches the cluster barriers after its bounded waits.
 #pragma once
 
 #include "ql_common.cuh"
