@@ -649,6 +649,8 @@ int ctas_per_sm(size_t smem) {
 struct GemmLaunch {
   int stages = 0, ks = 1, nk_split = 0, clusters_fit = 0;
   size_t smem = 0;
+  int stages_unsplit = 0;     // the plan without a K-split (fallback)
+  size_t smem_unsplit = 0;
 };
 
 template <int WBITS, int LAYOUT, int BN>
@@ -707,6 +709,8 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
   }
   g->nk_split = (int)cdiv(nk, ks);
   g->ks = (int)cdiv(nk, g->nk_split);
+  g->stages_unsplit = S;
+  g->smem_unsplit = L::smem_bytes(S);
   if (g->ks == 1) {
     g->stages = S;
     g->smem = L::smem_bytes(S);
@@ -724,8 +728,19 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
   prm.nk_split = g.nk_split;
   dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)g.ks);
   if (grid.y > 65535 || grid.z > 65535) return QL_ERR_BAD_SHAPE;
-  return launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem, a.stream,
-                   (a.flags & QL_FLAG_PDL) != 0, g.ks, tx, tw, prm);
+  const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
+  st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem, a.stream, pdl,
+                 g.ks, tx, tw, prm);
+  if (st == QL_ERR_CUDA && g.ks > 1) {
+    // a cluster launch the device refuses (resources taken by other work,
+    // a different partitioning): the same product unsplit
+    prm.stages = g.stages_unsplit;
+    prm.nk_split = prm.nk;
+    grid.z = 1;
+    st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem_unsplit,
+                   a.stream, pdl, 1, tx, tw, prm);
+  }
+  return st;
 }
 
 // The launch plan of the tensor-core kernel for (wbits, layout, M, N, K).
