@@ -444,22 +444,24 @@ __global__ void __launch_bounds__(kMaxThreads, 2)
           }
         }
       }
-    } else for (int v = ctid; v < nvec; v += nct) {
-      const bool in_k = kx0 + v * 8 < p.K;
-      #pragma unroll
-      for (int r0 = 0; r0 < MC; r0 += 8) {
-        uint4 val[8];
+    } else {
+      for (int v = ctid; v < nvec; v += nct) {
+        const bool in_k = kx0 + v * 8 < p.K;
         #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          val[u] = make_uint4(0u, 0u, 0u, 0u);
-          if (r0 + u < mvalid && in_k) val[u] = ldg_cg_v4(p.x + (long long)(m0 + r0 + u) * p.ldx + kx0 + v * 8);
-        }
-        #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (r0 + u < mvalid) {
-            uint4 w = val[u];
-            if (WBITS == 4) w = stage_x_perm<LAYOUT>(w);   // k order of the permuted int4 decode
-            *reinterpret_cast<uint4*>(xs + (r0 + u) * p.x_stride + v * 8) = w;
+        for (int r0 = 0; r0 < MC; r0 += 8) {
+          uint4 val[8];
+          #pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            val[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (r0 + u < mvalid && in_k) val[u] = ldg_cg_v4(p.x + (long long)(m0 + r0 + u) * p.ldx + kx0 + v * 8);
+          }
+          #pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (r0 + u < mvalid) {
+              uint4 w = val[u];
+              if (WBITS == 4) w = stage_x_perm<LAYOUT>(w);   // k order of the permuted int4 decode
+              *reinterpret_cast<uint4*>(xs + (r0 + u) * p.x_stride + v * 8) = w;
+            }
           }
         }
       }
