@@ -135,21 +135,21 @@ __device__ __forceinline__ float finish_value(const Params& p, float v, int n) {
 }
 
 // B fragments (activations) of one 64-byte k-step for MT batch tiles: the
-// two 16-element runs of row t*8+g that this lane's weights multiply.  Rows
-// past the batch stay zero (their outputs are never stored).
+// two 16-element runs of row t*8+g that this lane's weights multiply.  Lanes
+// of rows past the batch read row 0 instead: an mma output column depends
+// only on its own B column, and those columns are never stored — so no
+// predicate and no zeroing in the hot loop.
 template <int MT>
 __device__ __forceinline__ void load_b(uint32_t (&b0)[MT][8], uint32_t (&b1)[MT][8], uint32_t xs_s,
                                        int x_stride, int g, int mvalid, int e0, int e1) {
   #pragma unroll
   for (int t = 0; t < MT; ++t) {
-    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
-    if (t * 8 + g < mvalid) {
-      const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * x_stride) * 2u;
-      v0 = lds128(xr + e0 * 2);
-      v1 = lds128(xr + e0 * 2 + 16);
-      v2 = lds128(xr + e1 * 2);
-      v3 = lds128(xr + e1 * 2 + 16);
-    }
+    const int row = t * 8 + g < mvalid ? t * 8 + g : 0;
+    const uint32_t xr = xs_s + (uint32_t)(row * x_stride) * 2u;
+    const uint4 v0 = lds128(xr + e0 * 2);
+    const uint4 v1 = lds128(xr + e0 * 2 + 16);
+    const uint4 v2 = lds128(xr + e1 * 2);
+    const uint4 v3 = lds128(xr + e1 * 2 + 16);
     b0[t][0] = v0.x; b0[t][1] = v0.y; b0[t][2] = v0.z; b0[t][3] = v0.w;
     b0[t][4] = v1.x; b0[t][5] = v1.y; b0[t][6] = v1.z; b0[t][7] = v1.w;
     b1[t][0] = v2.x; b1[t][1] = v2.y; b1[t][2] = v2.z; b1[t][3] = v2.w;
@@ -253,12 +253,10 @@ __device__ __forceinline__ void ksteps(float (&acc)[2][MT][4], uint32_t rowA, ui
       const int e0 = i * kBlockBytes + (h0 + n) * 64 + 16 * c;
       #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
-        if (t * 8 + g < mvalid) {
-          const uint32_t xr = xs_s + (uint32_t)((t * 8 + g) * x_stride) * 2u;
-          v0 = lds128(xr + e0 * 2);
-          v1 = lds128(xr + e0 * 2 + 16);
-        }
+        const int row = t * 8 + g < mvalid ? t * 8 + g : 0;   // see load_b
+        const uint32_t xr = xs_s + (uint32_t)(row * x_stride) * 2u;
+        const uint4 v0 = lds128(xr + e0 * 2);
+        const uint4 v1 = lds128(xr + e0 * 2 + 16);
         bx[n][t][0] = v0.x; bx[n][t][1] = v0.y; bx[n][t][2] = v0.z; bx[n][t][3] = v0.w;
         bx[n][t][4] = v1.x; bx[n][t][5] = v1.y; bx[n][t][6] = v1.z; bx[n][t][7] = v1.w;
       }
