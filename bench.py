@@ -520,7 +520,8 @@ def layer_bytes(wbits, K, N):
 def run_sharded(args):
     """`--workload sharded`: BASELINE config 4.  Every rank holds its column
     shard of each layer (quantized on the device), runs the local kernel and
-    one NCCL all-gather of the fp16 outputs; for the lm_heads the greedy
+    an all-gather of the fp16 outputs — NCCL's, and the peer-memory kernel
+    (qlinear.p2p.PeerGather, which `value` is measured on); for the lm_heads the greedy
     head (argmax only) also runs with the per-row argmax keys exchanged over
     NVLink (qlinear.p2p) — up to 8 rows as ONE launch per rank (the decode
     kernel's epilogue makes the keys and runs the exchange), and, for
@@ -539,7 +540,7 @@ def run_sharded(args):
     import torch.distributed as dist
     from qlinear.kernels.w4a16_matmul import w4a16_quantize_cuda
     from qlinear.kernels.w8a16_matmul import w8a16_quantize_cuda
-    from qlinear.p2p import PeerExchange
+    from qlinear.p2p import PeerExchange, PeerGather
     from qlinear.quantization.int4 import QuantizedLinearInt4
     from qlinear.quantization.int8 import QuantizedLinearInt8
     from qlinear.sharded import ShardedQuantizedLinear, shard_bounds
@@ -607,6 +608,7 @@ def run_sharded(args):
                     sh.exchange = exchange     # argmax head: keys over NVLink, one kernel
                 shs.append(sh)
             iters = copies * max(1, math.ceil(16 / copies))
+            gatherer = PeerGather(rank, world, max_m=max(SHARDED_MS), n_cols=N)
             for M in SHARDED_MS:
                 x = torch.randn(M, K, generator=gen, device=dev).half()
                 with torch.cuda.stream(stream):
@@ -622,16 +624,25 @@ def run_sharded(args):
                     g_arg = capture(lambda i: shs[i % copies].argmax(x), iters) if groups == 1 else None
                     g_arg2 = (capture(lambda i: shs[i % copies].argmax(x, fused=False), iters)
                               if groups == 1 else None)
+                    for sh in shs:                       # the all-gather over NVLink peer memory
+                        sh.gatherer = gatherer
+                        sh(x)
+                    torch.cuda.synchronize(dev)
+                    g_p2p = capture(lambda i: shs[i % copies](x), iters)
+                    for sh in shs:
+                        sh.gatherer = None
                 t_loc, t_e2e = timed(g_loc, iters), timed(g_e2e, iters)
+                t_p2p = timed(g_p2p, iters)
                 t_col = timed(g_col, iters) if g_col is not None else 0.0
                 t_arg = timed(g_arg, iters) if g_arg is not None else None
                 t_arg2 = timed(g_arg2, iters) if g_arg2 is not None else None
                 # graphs holding NCCL calls must be gone before the process group is destroyed
                 torch.cuda.synchronize(dev)
-                del g_loc, g_col, g_e2e, g_arg, g_arg2
+                del g_loc, g_col, g_e2e, g_arg, g_arg2, g_p2p
                 if rank == 0:
                     print(f"[sharded] w{wbits} {name} M={M}: local {t_loc * 1e6:.1f} us, all-gather "
-                          f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us"
+                          f"{t_col * 1e6:.1f} us, end-to-end {t_e2e * 1e6:.1f} us (NCCL) / "
+                          f"{t_p2p * 1e6:.1f} us (peer all-gather)"
                           + (f", argmax head {t_arg * 1e6:.1f} us (two launches {t_arg2 * 1e6:.1f} us)"
                              if t_arg is not None else "")
                           + f" ({copies} copies, {iters} iterations per graph)",
@@ -639,14 +650,16 @@ def run_sharded(args):
                 lb = layer_bytes(wbits, K, N)
                 detail[f"w{wbits}_{name}_M{M}"] = {
                     "compute_us": round(t_loc * 1e6, 2), "allgather_us": round(t_col * 1e6, 2),
-                    "e2e_us": round(t_e2e * 1e6, 2), "GBps_e2e": round(lb / t_e2e / 1e9, 1),
+                    "e2e_nccl_us": round(t_e2e * 1e6, 2), "e2e_peer_us": round(t_p2p * 1e6, 2),
+                    "GBps_e2e": round(lb / t_p2p / 1e9, 1),
                     "GBps_compute_per_gpu": round(lb / world / t_loc / 1e9, 1)}
                 if t_arg is not None:
                     detail[f"w{wbits}_{name}_M{M}"]["argmax_us"] = round(t_arg * 1e6, 2)
                     detail[f"w{wbits}_{name}_M{M}"]["argmax_two_launch_us"] = round(t_arg2 * 1e6, 2)
                 tot_bytes += lb
-                tot_s += t_e2e
+                tot_s += t_p2p
             del shs
+            gatherer.close()
     exchange.close()
     from qlinear import _lib
     dev_err = _lib.device_error()
@@ -658,9 +671,10 @@ def run_sharded(args):
             "steps": reps, "warmup": 1, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "config4: column-sharded lm_head 1536->151936, lm_head 4096->128256, fused "
-                                   "gate+up 4096->28672 (2 groups), W4A16 and W8A16, M in {1,16,64}, NCCL "
-                                   "all-gather of fp16 outputs (argmax head: keys over NVLink), weight copies "
-                                   "cycled past L2",
+                                   "gate+up 4096->28672 (2 groups), W4A16 and W8A16, M in {1,16,64}; value "
+                                   "over the forward with the fp16 outputs all-gathered by the peer-memory "
+                                   "kernel (NCCL all-gather and argmax head, keys over NVLink, in detail), "
+                                   "weight copies cycled past L2",
                        "parallelism": f"column shards x{world}"},
             "detail": detail}), flush=True)
     if world > 1:

@@ -296,6 +296,29 @@ int ql_w4a16_linear_argmax(const void* x, int x_dtype, const void* w_packed, int
                            int max_m, void* const* peers, int64_t* out_ids, unsigned flags, void* stream);
 int ql_linear_argmax_supported(int wbits, int64_t M, int64_t N, int64_t K);
 
+/* ------------------------------------- sharded outputs: all-gather over NVLink */
+/* All-gather of a column-sharded layer's fp16 outputs, one launch per rank,
+ * no NCCL: the B200 build's replacement for the all-gather that a
+ * column-sharded lm_head / gate+up projection needs (the reference runs one
+ * GPU; its unsharded output is QuantizedLinearInt{8,4}.forward, int8.py:62,
+ * int4.py:61).  The output out [M, ldo] holds `groups` blocks of
+ * N / groups columns; rank q owns columns [q*block, min(N/groups,
+ * (q+1)*block)) of every block.  This rank's columns are either already in
+ * `out` (src = NULL) or in src [M, groups*w] (lds; w = this rank's width per
+ * block: gate columns, then up columns), then copied into out as well.  The
+ * kernel stores them into every peer's gather buffer over NVLink, signals
+ * with a system-scope release, waits (bounded) for every peer's signal and
+ * copies the peers' columns into out: on completion out holds all N columns
+ * on every rank.  All ranks make the same sequence of calls with the same
+ * shapes.  Gather buffers: ql_gather_buffer_bytes(max_m, N) bytes, allocated
+ * and shared with ql_xchg_alloc / ql_xchg_open / ql_xchg_close /
+ * ql_xchg_free as the exchange buffers above (peers[rank] = own).  A wait
+ * that runs out records QL_DEVICE_ERROR_PEER_WAIT. */
+size_t ql_gather_buffer_bytes(int max_m, int64_t N);
+int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64_t M, int64_t N, int groups,
+                     int64_t block, int rank, int world, int max_m, void* const* peers, unsigned flags,
+                     void* stream);
+
 /* ------------------------------------------------------------- diagnostics */
 const char* ql_strerror(int status);
 /* Version as (major << 16) | (minor << 8) | patch. */
@@ -305,7 +328,7 @@ int ql_version(void);
 #define QL_DEVICE_ERROR_EMPTY_WAIT  2   /* the producer waited too long for a free stage  */
 #define QL_DEVICE_ERROR_MMA_WAIT    3   /* a tensor-core completion wait ran out          */
 #define QL_DEVICE_ERROR_TMEM        4   /* tensor-memory allocation failed                */
-#define QL_DEVICE_ERROR_PEER_WAIT   5   /* another rank's argmax keys never arrived       */
+#define QL_DEVICE_ERROR_PEER_WAIT   5   /* another rank's keys / columns never arrived    */
 /* Kernels never trap: a bounded wait that runs out records a code in a
  * device-global word, and the kernel lets its copies in flight land and
  * returns early.  These read (and clear)

@@ -1,0 +1,199 @@
+// qgather.cuh — all-gather of a column-sharded layer's fp16 outputs over
+// NVLink peer memory, one kernel per rank, no NCCL.
+//
+// The output [M, N] is `groups` blocks of ng = N / groups columns (one block
+// for an lm_head, two for a fused [gate | up] projection); rank q owns the
+// columns [q*b, min(ng, (q+1)*b)) of every block, b = ceil(ng / world).
+//
+// Every rank owns a gather buffer (plain device memory shared with the other
+// ranks of the node through CUDA IPC, zero-filled at allocation):
+//   [0, 32)     flags[kMaxRanks] u32: the last call whose columns rank q has
+//               completely stored into this buffer (written by rank q)
+//   [32, 40)    state: counter u32 (CTAs arrived), epoch u32 (calls done);
+//               only the owner touches them
+//   [256, ...)  data[2][max_m][ldb] fp16, ldb = N rounded up to 8: the other
+//               ranks' columns of a call, by epoch parity, at their global
+//               positions
+//
+// One launch per rank and call, after the rank's own columns are in `out`
+// (or in `src`, then they are copied into `out` too):
+//   1. every CTA stores its share of the rank's columns into data[e & 1] of
+//      every peer (16-byte stores when the shapes allow), makes them visible
+//      system-wide (fence.sc.sys) and counts itself in;
+//   2. the last CTA to arrive writes e into flags[rank] of every peer with a
+//      system-scope release;
+//   3. every CTA takes the peers in turn: one thread polls (bounded, acquire)
+//      until the peer's flag reads e, then the CTA copies its share of that
+//      peer's columns from data[e & 1] into `out`.
+// A rank waits for every peer's flag of a call before it finishes the call,
+// so it is at most one call ahead of any peer: when it stores call e + 2
+// into a peer's bank e & 1, that peer has finished call e + 1, and with it
+// its copy out of call e's bank.  Two banks are therefore enough.  The grid
+// is at most one CTA per SM, so all CTAs of a rank are resident together and
+// no CTA waits on one that cannot run.  Ranks must make the same sequence of
+// calls.  A wait that runs out sets kDevErrPeerWait in the device error word
+// and the kernel carries on (the affected columns are then stale).
+#pragma once
+
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gather {
+
+constexpr int kMaxRanks = 8;
+
+struct Layout {
+  size_t flags, state, data, total;
+  long long ldb;
+};
+__host__ __device__ inline Layout layout(int max_m, long long n) {
+  Layout l;
+  l.flags = 0;
+  l.state = kMaxRanks * 4;
+  l.data = 256;
+  l.ldb = (n + 7) / 8 * 8;
+  l.total = (l.data + (size_t)2 * max_m * l.ldb * 2 + 255) / 256 * 256;
+  return l;
+}
+
+struct Params {
+  const __half* src;      // this rank's columns [M, groups*w] (ld lds), or nullptr: already in out
+  long long lds;
+  __half* out;            // [M, ldo]
+  long long ldo;
+  long long ng, block;    // columns per group; shard width per group
+  int M, groups, rank, world, max_m;
+  int vec;                // 16-byte path: 8-aligned offsets, widths and strides
+  unsigned char* peer[kMaxRanks];   // gather buffer of every rank (peer[rank] = own)
+  unsigned* err;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Columns of rank q within one group.
+__device__ __forceinline__ long long shard_width(const Params& p, int q) {
+  const long long c0 = (long long)q * p.block;
+  return c0 >= p.ng ? 0 : min(p.block, p.ng - c0);
+}
+
+// Unit i of rank q's [M, groups*w] slice (units of `vw` columns; i <
+// M*groups*wu) -> its row m, its column j within the slice and its global
+// column col, both in units.
+__device__ __forceinline__ void locate(int groups, long long ngu, long long bu, int q, long long wu, long long i,
+                                       int& m, long long& j, long long& col) {
+  const long long per_row = (long long)groups * wu;
+  m = (int)(i / per_row);
+  j = i - (long long)m * per_row;
+  const long long g = j / wu;
+  col = g * ngu + (long long)q * bu + (j - g * wu);
+}
+
+__global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
+  __shared__ unsigned done_s;
+  __shared__ int last_s;
+  griddep_wait();   // this rank's columns come from the kernel before
+
+  const Layout L = layout(p.max_m, (long long)p.groups * p.ng);
+  unsigned char* own = p.peer[p.rank];
+  unsigned* flags = reinterpret_cast<unsigned*>(own + L.flags);
+  unsigned* counter = reinterpret_cast<unsigned*>(own + L.state);
+  unsigned* epoch_done = counter + 1;
+  if (threadIdx.x == 0) done_s = *reinterpret_cast<volatile unsigned*>(epoch_done);
+  __syncthreads();
+  const unsigned e = done_s + 1u;
+  const size_t bank = (size_t)(e & 1u) * p.max_m * L.ldb;
+  const long long nthr = (long long)gridDim.x * blockDim.x;
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int vw = p.vec ? 8 : 1;   // elements per unit (ng and block are multiples of it)
+  const long long ngu = p.ng / vw, bu = p.block / vw;
+
+  // ---- 1. push this rank's columns to every peer (and into out if staged)
+  {
+    const long long wu = shard_width(p, p.rank) / vw;
+    const long long units = (long long)p.M * p.groups * wu;
+    for (long long i = tid; i < units; i += nthr) {
+      int m;
+      long long j, col;
+      locate(p.groups, ngu, bu, p.rank, wu, i, m, j, col);
+      col *= vw;
+      if (p.vec) {
+        const uint4 v = p.src ? *reinterpret_cast<const uint4*>(p.src + (long long)m * p.lds + j * 8)
+                              : __ldcg(reinterpret_cast<const uint4*>(p.out + (long long)m * p.ldo + col));
+        if (p.src) *reinterpret_cast<uint4*>(p.out + (long long)m * p.ldo + col) = v;
+        for (int k = 1; k < p.world; ++k) {
+          const int q = (p.rank + k) % p.world;
+          __half* dst = reinterpret_cast<__half*>(p.peer[q] + L.data) + bank + (long long)m * L.ldb + col;
+          *reinterpret_cast<uint4*>(dst) = v;
+        }
+      } else {
+        const __half v = p.src ? p.src[(long long)m * p.lds + j] : p.out[(long long)m * p.ldo + col];
+        if (p.src) p.out[(long long)m * p.ldo + col] = v;
+        for (int k = 1; k < p.world; ++k) {
+          const int q = (p.rank + k) % p.world;
+          reinterpret_cast<__half*>(p.peer[q] + L.data)[bank + (long long)m * L.ldb + col] = v;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();   // this CTA's peer stores, before it counts itself in
+    last_s = atomic_add_acq_rel_gpu(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+
+  // ---- 2. the last CTA: every CTA's stores are out, tell the peers
+  if (last_s && threadIdx.x == 0) {
+    *reinterpret_cast<volatile unsigned*>(counter) = 0u;        // all CTAs have arrived
+    *reinterpret_cast<volatile unsigned*>(epoch_done) = e;      // all CTAs have read it
+    __threadfence_system();
+    for (int k = 1; k < p.world; ++k) {
+      const int q = (p.rank + k) % p.world;
+      st_release_sys(reinterpret_cast<unsigned*>(p.peer[q] + L.flags) + p.rank, e);
+    }
+  }
+
+  // ---- 3. peers in turn: wait for the flag, copy the columns out
+  const __half* data = reinterpret_cast<const __half*>(own + L.data) + bank;
+  for (int k = 1; k < p.world; ++k) {
+    const int q = (p.rank + k) % p.world;
+    if (threadIdx.x == 0) {
+      const unsigned* f = flags + q;
+      if (ld_acquire_sys(f) != e) {
+        const long long t0 = clock64();
+        while (ld_acquire_sys(f) != e) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            atomicCAS(p.err, 0u, kDevErrPeerWait);
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+    }
+    __syncthreads();
+    const long long wu = shard_width(p, q) / vw;
+    const long long units = (long long)p.M * p.groups * wu;
+    for (long long i = tid; i < units; i += nthr) {
+      int m;
+      long long j, col;
+      locate(p.groups, ngu, bu, q, wu, i, m, j, col);
+      col *= vw;
+      if (p.vec) {
+        *reinterpret_cast<uint4*>(p.out + (long long)m * p.ldo + col) =
+            __ldcg(reinterpret_cast<const uint4*>(data + (long long)m * L.ldb + col));
+      } else {
+        p.out[(long long)m * p.ldo + col] = __ldcg(data + (long long)m * L.ldb + col);
+      }
+    }
+  }
+}
+
+}  // namespace gather
+}  // namespace ql

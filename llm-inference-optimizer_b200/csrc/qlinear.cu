@@ -21,6 +21,7 @@
 #include "ql_common.cuh"
 #include "qargmax.cuh"
 #include "qxchg.cuh"
+#include "qgather.cuh"
 #include "qformat.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
@@ -1345,6 +1346,54 @@ int ql_argmax_exchange_f16(const void* x, int64_t M, int64_t N, int64_t ldx, int
   p.err = dev->err_word;
   return launch(ql::xchg::argmax_exchange_kernel, dim3((unsigned)cdiv(N, p.span), (unsigned)M), dim3(256), 0,
                 static_cast<cudaStream_t>(stream), true, p);
+}
+
+size_t ql_gather_buffer_bytes(int max_m, int64_t N) {
+  if (max_m < 1 || max_m > 65535 || N < 1 || N > INT_MAX) return 0;
+  return ql::gather::layout(max_m, N).total;
+}
+
+int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64_t M, int64_t N, int groups,
+                     int64_t block, int rank, int world, int max_m, void* const* peers, unsigned flags,
+                     void* stream) {
+  if (!out || !peers) return QL_ERR_NULL_POINTER;
+  if (world < 1 || world > QL_XCHG_MAX_RANKS || rank < 0 || rank >= world) return QL_ERR_BAD_SHAPE;
+  if (groups < 1 || M < 1 || M > max_m || max_m > 65535 || N < 1 || N > INT_MAX || N % groups != 0)
+    return QL_ERR_BAD_SHAPE;
+  const int64_t ng = N / groups;
+  if (block < 1 || block * world < ng) return QL_ERR_BAD_SHAPE;   // the shards must cover a block
+  const int64_t c0 = (int64_t)rank * block;
+  const int64_t w = c0 >= ng ? 0 : std::min<int64_t>(block, ng - c0);
+  if (ldo < N) return QL_ERR_BAD_STRIDE;
+  if (src && lds < groups * w) return QL_ERR_BAD_STRIDE;
+  for (int q = 0; q < world; ++q)
+    if (!peers[q]) return QL_ERR_NULL_POINTER;
+  if (world == 1 && !src) return QL_OK;   // nothing to move
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  if (!dev) return st;
+  ql::gather::Params p{};
+  p.src = static_cast<const __half*>(src);
+  p.lds = lds;
+  p.out = static_cast<__half*>(out);
+  p.ldo = ldo;
+  p.ng = ng;
+  p.block = block;
+  p.M = (int)M;
+  p.groups = groups;
+  p.rank = rank;
+  p.world = world;
+  p.max_m = max_m;
+  p.vec = aligned16(out) && ldo % 8 == 0 && ng % 8 == 0 && block % 8 == 0 &&
+          (!src || (aligned16(src) && lds % 8 == 0));
+  for (int q = 0; q < world; ++q) p.peer[q] = static_cast<unsigned char*>(peers[q]);
+  p.err = dev->err_word;
+  // one CTA per SM at most (every CTA waits on the peers: all must be
+  // resident together), fewer when there is little to move
+  const int64_t units = M * N / (p.vec ? 8 : 1);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(dev->sms, cdiv(units, 512 * 4)));
+  return launch(ql::gather::allgather_kernel, dim3((unsigned)grid), dim3(512), 0, static_cast<cudaStream_t>(stream),
+                (flags & QL_FLAG_PDL) != 0, p);
 }
 
 // Once per device, with that device current: the host-side name of

@@ -89,6 +89,9 @@ SIGNATURES = {
     "ql_w4a16_linear_argmax": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _i64, _int, _int, _int, ctypes.POINTER(_vp), _vp, _uint, _vp]),
     "ql_linear_argmax_supported": (_int, [_int, _i64, _i64, _i64]),
+    "ql_gather_buffer_bytes": (_sz, [_int, _i64]),
+    "ql_allgather_f16": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _i64, _int, _int, _int,
+                                ctypes.POINTER(_vp), _uint, _vp]),
     "ql_strerror": (ctypes.c_char_p, [_int]),
     "ql_version": (_int, []),
     "ql_device_error": (_int, [ctypes.POINTER(_int)]),

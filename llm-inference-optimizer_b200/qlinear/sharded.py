@@ -4,8 +4,10 @@ Large-N layers (the lm_head, a fused gate+up projection) are split by
 output column: rank p of P holds the weight rows (output columns)
 [p*Np, (p+1)*Np) with Np = ceil(N/P) (the last shard may be short), runs the
 unchanged single-GPU quantized linear on its rows, and one all-gather of the
-fp16 outputs over NVLink (NCCL, through ``torch.distributed``) rebuilds the
-full [M, N] result on every rank.
+fp16 outputs over NVLink rebuilds the full [M, N] result on every rank:
+NCCL through ``torch.distributed`` by default, or, with a
+``qlinear.p2p.PeerGather`` attached as ``gatherer``, one kernel per rank that
+stores the columns into the peers' memory itself.
 
 ``groups`` handles layers whose output is a concatenation of equally sized
 blocks that must be sharded alike — a fused gate+up projection [gate; up]
@@ -54,11 +56,12 @@ def _group_cols(t: torch.Tensor, groups: int, rank: int, world: int) -> torch.Te
     return torch.cat([t[:, g * n + lo:g * n + hi] for g in range(groups)], dim=1).contiguous()
 
 
-def local_linear_cuda(module: nn.Module, x: torch.Tensor) -> torch.Tensor:
-    """The shard's own compute: the single-GPU B200 kernels."""
+def local_linear_cuda(module: nn.Module, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The shard's own compute: the single-GPU B200 kernels (into `out`, a
+    [M, N_local] view with unit inner stride, when given)."""
     if isinstance(module, QuantizedLinearInt4):
-        return w4a16_linear(x, module.weight_packed, module.scales, module.bias, layout=module.layout)
-    return w8a16_linear(x, module.weight_q, module.scale, module.bias)
+        return w4a16_linear(x, module.weight_packed, module.scales, module.bias, layout=module.layout, out=out)
+    return w8a16_linear(x, module.weight_q, module.scale, module.bias, out=out)
 
 
 class ShardedQuantizedLinear(nn.Module):
@@ -80,6 +83,7 @@ class ShardedQuantizedLinear(nn.Module):
         self.local_fn = local_fn
         self.key_fn = key_fn
         self.exchange = None          # optional qlinear.p2p.PeerExchange for argmax
+        self.gatherer = None          # optional qlinear.p2p.PeerGather for forward
         n = out_features // groups
         self.block = (n + world - 1) // world          # padded per-rank width of one group
         self.widths = [shard_bounds(n, r, world)[1] - shard_bounds(n, r, world)[0] for r in range(world)]
@@ -183,5 +187,21 @@ class ShardedQuantizedLinear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         K = self.in_features
         x2 = x.reshape(-1, K)
+        M = x2.shape[0]
+        g = self.gatherer
+        if (g is not None and self.local_fn is local_linear_cuda and x2.dtype == torch.float16
+                and 1 <= M <= g.max_m):
+            # all-gather over NVLink peer memory: the shard's kernel writes
+            # its columns straight into the full output (one block), or into
+            # a [gate | up] staging tensor that the gather kernel spreads
+            out = torch.empty((M, self.out_features), dtype=x2.dtype, device=x2.device)
+            if self.groups == 1:
+                lo, hi = shard_bounds(self.out_features, self.rank, self.world)
+                if hi > lo:
+                    local_linear_cuda(self.local, x2, out=out[:, lo:hi])
+                g.gather(out, self.block)
+            else:
+                g.gather(out, self.block, self.groups, src=self.local_fn(self.local, x2))
+            return out.reshape(*x.shape[:-1], self.out_features)
         out = self.gather(self.local_forward(x2))
         return out.reshape(*x.shape[:-1], self.out_features)

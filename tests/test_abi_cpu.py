@@ -108,6 +108,36 @@ def test_greedy_head_argument_checks_without_gpu():
     assert lib.ql_linear_argmax_supported(4, 1, 4096, 100) == 0
 
 
+def test_gather_argument_checks_without_gpu():
+    """The NVLink all-gather checks shapes, strides and peers on the host;
+    its buffer size covers two banks of [max_m, N rounded up to 8] fp16."""
+    import ctypes
+    lib = _lib.load()
+    assert lib.ql_gather_buffer_bytes(0, 1024) == 0
+    assert lib.ql_gather_buffer_bytes(4, 0) == 0
+    assert lib.ql_gather_buffer_bytes(4, 1001) >= 256 + 2 * 4 * 1008 * 2
+    assert lib.ql_gather_buffer_bytes(4, 1001) % 256 == 0
+    names = ["src", "lds", "out", "ldo", "M", "N", "groups", "block", "rank", "world", "max_m", "peers",
+             "flags", "stream"]
+    ok = dict(zip(names, (None, 0, 1, 4096, 2, 4096, 1, 2048, 0, 2, 4, (ctypes.c_void_p * 2)(1, 1), 0, None)))
+
+    def call(**kw):
+        args = dict(ok, **kw)
+        return lib.ql_allgather_f16(*[args[n] for n in names])
+
+    assert call(out=None) == _lib.QL_ERR_NULL_POINTER
+    assert call(peers=(ctypes.c_void_p * 2)(1, None)) == _lib.QL_ERR_NULL_POINTER
+    assert call(world=9) == _lib.QL_ERR_BAD_SHAPE
+    assert call(rank=2) == _lib.QL_ERR_BAD_SHAPE
+    assert call(M=5) == _lib.QL_ERR_BAD_SHAPE                 # beyond max_m
+    assert call(block=2000) == _lib.QL_ERR_BAD_SHAPE          # two shards do not cover 4096 columns
+    assert call(N=4095, groups=2) == _lib.QL_ERR_BAD_SHAPE    # groups must divide N
+    assert call(ldo=4000) == _lib.QL_ERR_BAD_STRIDE
+    assert call(src=1, lds=1000) == _lib.QL_ERR_BAD_STRIDE    # this rank's 2048 columns need lds >= 2048
+    # one rank with its columns already in place: nothing to launch
+    assert call(world=1, block=4096, peers=(ctypes.c_void_p * 1)(1)) == 0
+
+
 def test_pack_unpack_roundtrip():
     """The reference's KAT (tests/test_w4a16_kernel.py:52-59)."""
     torch.manual_seed(0)

@@ -2,7 +2,9 @@
 
 Each rank runs the B200 kernels on its shard; the all-gathered output must
 match the CPU oracle of the full layer, eagerly and replayed from a CUDA
-graph that contains the kernel and the NCCL collective.
+graph that contains the kernel and the NCCL collective.  The all-gather over
+NVLink peer memory (PeerGather) must give the same bits as NCCL's, over
+consecutive calls with changing inputs and from graph replays.
 """
 import datetime
 import os
@@ -92,6 +94,32 @@ def _worker(rank, world, port, case, result_q):
             sh.exchange.close()
             from qlinear import _lib
             same = same and _lib.device_error() == 0
+        # the all-gather over peer memory: same bits as NCCL's, call after
+        # call (the two banks alternate) and from graph replays
+        from qlinear.p2p import PeerGather
+        xs = [torch.randn(M, K, generator=g).half().cuda() for _ in range(3)]
+        want = [sh(xi) for xi in xs]
+        sh.gatherer = PeerGather(rank, world, max_m=64, n_cols=N)
+        for i in range(5):
+            same = same and torch.equal(sh(xs[i % 3]), want[i % 3])
+        xstat = xs[0].clone()
+        with torch.cuda.stream(s):
+            sh(xstat)
+            torch.cuda.synchronize()
+            g3 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g3, stream=s):
+                yp = sh(xstat)
+        torch.cuda.current_stream().wait_stream(s)
+        for i in range(5):
+            xstat.copy_(xs[(i + 1) % 3])
+            g3.replay()
+            torch.cuda.synchronize()
+            same = same and torch.equal(yp, want[(i + 1) % 3])
+        del g3
+        sh.gatherer.close()
+        sh.gatherer = None
+        from qlinear import _lib
+        same = same and _lib.device_error() == 0
         del graph
         dist.barrier()
         dist.destroy_process_group()
