@@ -128,8 +128,11 @@ def _worker(rank, world, port, case, result_q):
         result_q.put((rank, False, repr(e)[:300], None))
 
 
+# the peer all-gather sends the first case through its flagged banks 2 bytes
+# at a time (odd widths), the last one with 16-byte stores (5 MB of output),
+# the others as tagged lines
 @pytest.mark.parametrize("case", [(1536, 8192 + 37, 1, 4, 1), (4096, 2 * 1792, 16, 8, 2), (1536, 4096, 64, 4, 1),
-                                  (4096, 16032 * 2, 3, 8, 1)])
+                                  (4096, 16032 * 2, 3, 8, 1), (1536, 40960, 64, 4, 1)])
 def test_sharded_nccl_two_gpus(case):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
