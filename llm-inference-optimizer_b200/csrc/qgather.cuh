@@ -23,7 +23,8 @@
 // store carries 8 bytes of columns and the epoch twice, a reader polls each
 // word (bounded) until both tags read e, so neither side needs a fence, a
 // counter or a flag — twice the bytes on NVLink, a few microseconds less
-// latency.  Larger calls use the flagged protocol:
+// latency (used only when every rank owns columns: each rank then waits for
+// every peer's lines of a call).  Larger calls use the flagged protocol:
 //   1. every CTA stores its share of the rank's columns into data[e & 1] of
 //      every peer (16-byte stores when the shapes allow), makes them visible
 //      system-wide (fence.sc.sys) and counts itself in;

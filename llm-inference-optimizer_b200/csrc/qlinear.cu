@@ -1387,9 +1387,13 @@ int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64
   p.vec = aligned16(out) && ldo % 8 == 0 && ng % 8 == 0 && block % 8 == 0 &&
           (!src || (aligned16(src) && lds % 8 == 0));
   // small calls as tagged lines (8-byte column runs: 4-aligned offsets,
-  // widths and strides), the rest through the flagged banks
+  // widths and strides), the rest through the flagged banks.  Lines only
+  // when every rank owns columns: a reader waits for the lines of each peer
+  // that has some, and those waits are what keep every rank within one call
+  // of the others (a rank with none would never be waited for)
   const ql::gather::Layout L = ql::gather::layout(max_m, N);
-  p.lines = world > 1 && M <= L.line_rows && M * N * 2 <= ql::gather::kLineMaxPayload &&
+  p.lines = world > 1 && (int64_t)(world - 1) * block < ng && M <= L.line_rows &&
+            M * N * 2 <= ql::gather::kLineMaxPayload &&
             (reinterpret_cast<uintptr_t>(out) & 7u) == 0 && ldo % 4 == 0 && ng % 4 == 0 && block % 4 == 0 &&
             (!src || ((reinterpret_cast<uintptr_t>(src) & 7u) == 0 && lds % 4 == 0));
   for (int q = 0; q < world; ++q) p.peer[q] = static_cast<unsigned char*>(peers[q]);
