@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py — weight-only quantized GEMV throughput on B200.
 
-Workload (the configuration the metric is quoted
+Workload (benchmark config 1, the configuration the metric is quoted
 on): W4A16 group-128 GEMV / skinny GEMM, x fp16 [M, K] ~ N(0,1) with M in
 {1, 8, 32}, (K, N) in {(1536, 8960), (8960, 1536)}, W ~ N(0, 0.02) quantized
 by the reference's RTN quantizer into the reference's packed format.
@@ -439,7 +439,7 @@ PREFILL_SHAPES = ((1536, 8960), (8960, 1536), (4096, 14336), (14336, 4096))   # 
 
 
 def prefill_measure(reps=5, wbits_list=(4, 8), ms=PREFILL_MS, shapes=PREFILL_SHAPES):
-    """dequant-fused GEMM on the tensor cores.  Per
+    """benchmark config 3: dequant-fused GEMM on the tensor cores.  Per
     (wbits, shape, M): best of `reps` CUDA-event timings of one launch, with
     L2 flushed (256 MB write) before every timed launch.  Returns
     {key: {"us": t, "TFLOPS": 2MNK/t}} and the aggregate TFLOPS."""
@@ -483,7 +483,7 @@ def prefill_measure(reps=5, wbits_list=(4, 8), ms=PREFILL_MS, shapes=PREFILL_SHA
 
 
 def run_prefill(args):
-    """`--workload prefill`: BASELINE config 3 as its own JSON line."""
+    """`--workload prefill`: benchmark config 3 as its own JSON line."""
     import torch
     torch.cuda.set_device(0)
     detail, agg = prefill_measure(reps=max(3, args.steps))
@@ -518,7 +518,7 @@ def layer_bytes(wbits, K, N):
 
 
 def run_sharded(args):
-    """`--workload sharded`: BASELINE config 4.  Every rank holds its column
+    """`--workload sharded`: benchmark config 4.  Every rank holds its column
     shard of each layer (quantized on the device), runs the local kernel and
     an all-gather of the fp16 outputs — NCCL's, and the peer-memory kernel
     (qlinear.p2p.PeerGather, which `value` is measured on); for the lm_heads the greedy
@@ -713,7 +713,7 @@ def decode_step_bytes(wbits, M, fused):
 
 
 def run_decode_step(args):
-    """`--workload decode_step`: BASELINE config 2.  The seven projections of
+    """`--workload decode_step`: benchmark config 2.  The seven projections of
     all 28 layers of a random-init Qwen2.5-1.5B (q/k/v with bias), quantized
     on the device, run through the public modules for one decode step at M
     in {1, 4, 16, 64}, W4 and W8 — once as seven launches per layer (the

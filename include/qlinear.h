@@ -167,8 +167,9 @@ int ql_gemm_plan(int wbits, int layout, int64_t M, int64_t N, int64_t K, int64_t
  *   - It never calls cudaMalloc, cudaFree or any allocating routine.
  *   - Shapes whose fastest plan needs more scratch than QL_STATIC_WS_BYTES
  *     return QL_ERR_WORKSPACE and launch nothing.
- *   - The first call on a device looks up the array's device address and
- *     clears it on `stream`; make that first call before any stream capture.
+ *   - The first call on a device looks up the array's device address,
+ *     clears it on `stream` and waits for the clear (so later calls on any
+ *     stream see it zeroed); make that first call before any stream capture.
  *   - All calls on a device share the array.  Each call leaves it zeroed for
  *     the next, but calls that overlap on the GPU (e.g. on two streams) race.
  */

@@ -31,12 +31,16 @@
 //   2. the last CTA to arrive writes e into flags[rank] of every peer with a
 //      system-scope release;
 //   3. every CTA takes the peers in turn: one thread polls (bounded, acquire)
-//      until the peer's flag reads e, then the CTA copies its share of that
+//      until the peer's flag has reached e, then the CTA copies its share of that
 //      peer's columns from data[e & 1] into `out`.
 // A rank waits for every peer's flag of a call before it finishes the call,
 // so it is at most one call ahead of any peer: when it stores call e + 2
 // into a peer's bank e & 1, that peer has finished call e + 1, and with it
-// its copy out of call e's bank.  Two banks are therefore enough.  The grid
+// its copy out of call e's bank.  Two banks are therefore enough.  The same
+// bound means a waiting rank may find a peer's flag already at e + 1 (the
+// peer finished call e and stored call e + 1 into the other bank), so the
+// wait is for the flag to have reached e (wrap-safe: (int)(flag - e) >= 0),
+// not for it to equal e.  The grid
 // is at most one CTA per SM, so all CTAs of a rank are resident together and
 // no CTA waits on one that cannot run.  Ranks must make the same sequence of
 // calls.  A wait that runs out sets kDevErrPeerWait in the device error word
@@ -90,6 +94,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+
+// A peer's flag has reached call e (it may already be at e + 1, never
+// further: see the header); wrap-safe over the 32-bit epoch.
+__device__ __forceinline__ bool flag_reached(unsigned flag, unsigned e) { return (int)(flag - e) >= 0; }
 
 // Columns of rank q within one group.
 __device__ __forceinline__ long long shard_width(const Params& p, int q) {
@@ -259,9 +267,9 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
     const int q = (p.rank + k) % p.world;
     if (threadIdx.x == 0) {
       const unsigned* f = flags + q;
-      if (ld_acquire_sys(f) != e) {
+      if (!flag_reached(ld_acquire_sys(f), e)) {
         const long long t0 = clock64();
-        while (ld_acquire_sys(f) != e) {
+        while (!flag_reached(ld_acquire_sys(f), e)) {
           if (clock64() - t0 > kWaitBudgetCycles) {
             atomicCAS(p.err, 0u, kDevErrPeerWait);
             break;

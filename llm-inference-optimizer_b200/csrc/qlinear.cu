@@ -1408,7 +1408,9 @@ int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64
 
 // Once per device, with that device current: the host-side name of
 // g_ql_static_ws is only a stand-in, so its device address is looked up
-// here, checked, and the array is cleared on the first caller's stream.
+// here and checked.  The array is zero when the module loads; the set-up
+// clears it once more on the first caller's stream and waits for that
+// clear, so calls made later on any stream find it zeroed.
 struct StaticWs {
   std::once_flag once;
   int status = QL_OK;
@@ -1437,7 +1439,8 @@ int ql_w4a16_linear_static_ws(const void* x, int x_dtype, const void* w_packed, 
       w.status = QL_ERR_CUDA;
       return;
     }
-    if (cudaMemsetAsync(ptr, 0, QL_STATIC_WS_BYTES, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    if (cudaMemsetAsync(ptr, 0, QL_STATIC_WS_BYTES, static_cast<cudaStream_t>(stream)) != cudaSuccess ||
+        cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
       cudaGetLastError();
       w.status = QL_ERR_CUDA;
       return;

@@ -33,22 +33,21 @@ LAYOUT_ADJACENT = _lib.QL_W4_LAYOUT_ADJACENT
 
 # ---------------------------------------------------------------- packing
 def pack_int4(q: torch.Tensor) -> torch.Tensor:
-    """q: (N, K) integer tensor with values in [0, 15] (offset-binary),
-    K % 128 == 0. Returns (N, K//2) uint8 in the split-half layout."""
+    """Pack 4-bit codes (values 0..15, shape [N, K], K a multiple of 128)
+    into [N, K/2] bytes, split-half within every 128-group: byte j of a group
+    carries code j in bits 0-3 and code j + 64 in bits 4-7."""
     N, K = q.shape
     assert K % GROUP_SIZE == 0, f"K={K} must be a multiple of {GROUP_SIZE}"
-    g = q.to(torch.uint8).reshape(N, K // GROUP_SIZE, 2, HALF)
-    packed = g[:, :, 0, :] | (g[:, :, 1, :] << 4)
-    return packed.reshape(N, K // 2).contiguous()
+    first, second = q.to(torch.uint8).reshape(N, K // GROUP_SIZE, 2, HALF).unbind(dim=2)
+    return (first | (second << 4)).reshape(N, K // 2).contiguous()
 
 
 def unpack_int4(packed: torch.Tensor) -> torch.Tensor:
-    """Inverse of pack_int4: (N, K//2) uint8 -> (N, K) uint8 in [0, 15]."""
+    """Codes of a split-half packed [N, K/2] byte tensor, as uint8 [N, K]:
+    per group of 64 bytes, the 64 low nibbles followed by the 64 high ones."""
     N, half_k = packed.shape
-    p = packed.reshape(N, half_k // HALF, HALF)
-    lo = p & 0xF
-    hi = p >> 4
-    return torch.stack([lo, hi], dim=2).reshape(N, half_k * 2)
+    per_group = packed.reshape(N, half_k // HALF, HALF)
+    return torch.cat((per_group & 0xF, per_group >> 4), dim=2).reshape(N, 2 * half_k)
 
 
 def pack_int4_adjacent(q: torch.Tensor) -> torch.Tensor:

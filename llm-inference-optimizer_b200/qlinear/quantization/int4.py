@@ -1,29 +1,52 @@
-"""INT4 group-wise weight quantization of a loaded model (W4A16, g=128).
+"""W4A16 module: 4-bit weights in groups of 128 along K, fp16 group scales.
 
-Drop-in for src/quantization/int4.py of the reference: the class, buffer
-names (``weight_packed``, ``scales``, ``bias``), ``from_linear`` (:37-49),
-``dequantized_weight`` (:51-52), ``num_bytes`` (:54-59), ``forward``
-(:61-62) and ``quantize_model_int4`` (:72-97) keep their behaviour.
-Plain round-to-nearest with max-abs group scales, as in the reference.
+Stands in for the reference's ``src/quantization/int4.py`` without any change
+visible to its callers.  Kept as the reference has them, because the engines,
+``state_dict`` and the reference's tests depend on them:
 
-Two optional keyword arguments select the variant format (q in [-8, 7],
-adjacent-pair nibbles); their defaults are the reference's format.
+* the class name and constructor ``(packed, scales, bias)``, and the buffer
+  names ``weight_packed`` (uint8 [N, K/2]), ``scales`` (fp16 [K/128, N]) and
+  ``bias`` (``int4.py:29-35``);
+* ``from_linear``'s arithmetic (``int4.py:37-49``), bit for bit: the group
+  scale is max|w| / 7 floored at 1e-5 and rounded to fp16 *before* the
+  weights are divided by it; codes are round-half-even, clamped, offset by 8;
+* ``dequantized_weight`` / ``num_bytes`` / ``forward`` (``:51-62``) and
+  ``quantize_model_int4``'s return value (``:72-97``).
+
+``forward`` runs the sm_100a kernels of libqlinear.so through
+``w4a16_linear``.  Two keyword arguments, both defaulting to the reference's
+format, select the variant that the benchmark's config 1 describes: codes down to
+-8 (``qmin=-8``) and adjacent-pair nibbles (``layout=LAYOUT_ADJACENT``).
 """
-import gc
 from typing import Optional
 
 import torch
 import torch.nn as nn
 
 from ..kernels.w4a16_matmul import (
-    GROUP_SIZE, LAYOUT_SPLIT_HALF, LAYOUT_ADJACENT, dequantize_int4, pack_int4,
-    pack_int4_adjacent, w4a16_linear, w4a16_quantize_cuda,
+    GROUP_SIZE, LAYOUT_ADJACENT, LAYOUT_SPLIT_HALF, dequantize_int4, pack_int4, pack_int4_adjacent,
+    w4a16_linear, w4a16_quantize_cuda,
 )
+from ._replace import replace_linears, tensor_bytes
+
+
+def _quantize_groups_torch(weight: torch.Tensor, qmin: int, layout: int):
+    """PyTorch form of the group quantizer (any device or dtype): returns
+    (packed uint8 [N, K/2], scales fp16 [K/128, N])."""
+    n_out, n_in = weight.shape
+    groups = weight.float().reshape(n_out, n_in // GROUP_SIZE, GROUP_SIZE)
+    step16 = torch.clamp(groups.abs().amax(dim=-1) / 7.0, min=1e-5).to(torch.float16)
+    codes = torch.round(groups / step16.float().unsqueeze(-1)).clamp(qmin, 7) + 8
+    codes = codes.to(torch.uint8).reshape(n_out, n_in)
+    pack = pack_int4 if layout == LAYOUT_SPLIT_HALF else pack_int4_adjacent
+    return pack(codes), step16.transpose(0, 1).contiguous()
 
 
 class QuantizedLinearInt4(nn.Module):
-    """Drop-in nn.Linear replacement: packed 4-bit weights, fp16 group
-    scales of shape (K//128, N), optional bias.  Inference-only buffers."""
+    """Inference-only replacement for an ``nn.Linear`` whose weight is held as
+    packed 4-bit codes with one fp16 scale per 128 inputs of each output.
+    Everything is a registered buffer (no Parameters), so ``state_dict``
+    carries the packed form."""
 
     def __init__(self, packed: torch.Tensor, scales: torch.Tensor, bias: Optional[torch.Tensor],
                  layout: int = LAYOUT_SPLIT_HALF):
@@ -32,80 +55,42 @@ class QuantizedLinearInt4(nn.Module):
         self.register_buffer("scales", scales)
         self.register_buffer("bias", bias)
         self.out_features = packed.shape[0]
-        self.in_features = packed.shape[1] * 2
+        self.in_features = 2 * packed.shape[1]
         self.layout = layout
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, qmin: int = -7,
                     layout: int = LAYOUT_SPLIT_HALF) -> "QuantizedLinearInt4":
-        """scale = max(|W[n, group]|)/7 (>= 1e-5) stored fp16; q =
-        round-half-even(W / float(scale16)) clamped to [qmin, 7]; nibble q+8.
-        On a CUDA fp16 weight the device quantizer produces the same bits as
-        the PyTorch expression used otherwise."""
-        wt = linear.weight.detach()
-        N, K = wt.shape
+        """Quantize ``linear`` group by group (codes in [qmin, 7] plus 8).  A
+        CUDA fp16 weight is quantized by the device kernel, which yields the
+        same bytes as the PyTorch form used for every other input."""
+        weight = linear.weight.detach()
+        N, K = weight.shape
         assert K % GROUP_SIZE == 0, f"in_features {K} must be a multiple of {GROUP_SIZE}"
-        if wt.is_cuda and wt.dtype == torch.float16 and N > 0:
-            packed, scales = w4a16_quantize_cuda(wt, qmin=qmin, layout=layout)
+        if weight.is_cuda and weight.dtype == torch.float16 and N > 0:
+            packed, scales = w4a16_quantize_cuda(weight, qmin=qmin, layout=layout)
         else:
-            w = wt.float()                                              # (N, K)
-            wg = w.reshape(N, K // GROUP_SIZE, GROUP_SIZE)
-            scale = (wg.abs().amax(dim=2) / 7.0).clamp(min=1e-5)          # (N, G)
-            scale16 = scale.half()                                        # what is actually stored
-            q = torch.round(wg / scale16.float()[:, :, None]).clamp(qmin, 7) + 8
-            q = q.reshape(N, K).to(torch.uint8)
-            packed = pack_int4(q) if layout == LAYOUT_SPLIT_HALF else pack_int4_adjacent(q)
-            scales = scale16.t().contiguous()                             # (G, N)
-        bias = linear.bias.detach().clone() if linear.bias is not None else None
+            packed, scales = _quantize_groups_torch(weight, qmin, layout)
+        bias = None if linear.bias is None else linear.bias.detach().clone()
         return cls(packed, scales, bias, layout=layout)
 
     def dequantized_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """The weight the kernels multiply by, as a dense [N, K] tensor."""
         return dequantize_int4(self.weight_packed, self.scales, self.layout).to(dtype)
 
     def num_bytes(self) -> int:
-        total = self.weight_packed.numel() * self.weight_packed.element_size()
-        total += self.scales.numel() * self.scales.element_size()
-        if self.bias is not None:
-            total += self.bias.numel() * self.bias.element_size()
-        return total
+        """Bytes held on the device: packed codes, group scales and bias."""
+        return tensor_bytes(self.weight_packed, self.scales, self.bias)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return w4a16_linear(x, self.weight_packed, self.scales, self.bias, layout=self.layout)
 
 
-def _linear_bytes(linear: nn.Linear) -> int:
-    total = linear.weight.numel() * linear.weight.element_size()
-    if linear.bias is not None:
-        total += linear.bias.numel() * linear.bias.element_size()
-    return total
-
-
 def quantize_model_int4(model: nn.Module) -> dict:
-    """Replaces every nn.Linear inside model.model.layers with a
-    QuantizedLinearInt4, in place.  Returns stats; callers should check
-    layers_quantized > 0."""
-    layers_quantized = 0
-    bytes_before = 0
-    bytes_after = 0
-
-    for parent in list(model.model.layers.modules()):
-        for child_name, child in list(parent.named_children()):
-            if isinstance(child, nn.Linear):
-                bytes_before += _linear_bytes(child)
-                quantized = QuantizedLinearInt4.from_linear(child)
-                bytes_after += quantized.num_bytes()
-                setattr(parent, child_name, quantized)
-                layers_quantized += 1
-
-    gc.collect()
-    if torch.cuda.is_available():
-        torch.cuda.empty_cache()
-
-    return {
-        "layers_quantized": layers_quantized,
-        "bytes_before": bytes_before,
-        "bytes_after": bytes_after,
-    }
+    """Put a ``QuantizedLinearInt4`` in place of every linear projection of the
+    decoder layers (``model.model.layers``); see ``replace_linears`` for the
+    returned statistics."""
+    return replace_linears(model, QuantizedLinearInt4.from_linear)
 
 
 __all__ = ["QuantizedLinearInt4", "quantize_model_int4", "LAYOUT_SPLIT_HALF", "LAYOUT_ADJACENT"]

@@ -34,7 +34,7 @@ HALF = GROUP_SIZE // 2    # w4a16_matmul_triton.py:38
 
 # Layout ids shared with the C-ABI (include/qlinear.h).
 LAYOUT_SPLIT_HALF = 0     # the reference's packing (w4a16_matmul_triton.py:10-20)
-LAYOUT_ADJACENT = 1       # low nibble = even k (the variant BASELINE config 1 describes)
+LAYOUT_ADJACENT = 1       # low nibble = even k (the variant benchmark config 1 describes)
 
 
 # --------------------------------------------------------------------- INT8
@@ -61,7 +61,7 @@ def dequantize_int8(w_q: np.ndarray, scale: np.ndarray) -> np.ndarray:
 
     Follows ``QuantizedLinearInt8.dequantized_weight`` (int8.py:52-53) and the
     first line of ``w8a16_reference`` (w8a16_matmul_triton.py:147).  The scale
-    may be fp32 (the reference's buffer) or fp16.
+    may be fp32 (the reference's buffer) or fp16 (benchmark config 0).
     """
     return w_q.astype(np.float32) * np.asarray(scale).astype(np.float32)[:, None]
 
@@ -117,7 +117,7 @@ def unpack_int4(packed: np.ndarray) -> np.ndarray:
 def pack_int4_adjacent(q: np.ndarray) -> np.ndarray:
     """Adjacent-pair packing: byte i holds k=2i (low nibble) and 2i+1 (high).
 
-    The reference has no code for this layout; it is the format BASELINE
+    The reference has no code for this layout; it is the format benchmark
     config 1 words ("two nibbles per uint8 along K, low nibble = even k").
     Nibble values are the same offset-binary q+8 as the reference's.
     """
@@ -159,7 +159,7 @@ def quantize_int4_groups(w: np.ndarray, qmin: int = -7, qmax: int = 7,
     ``scale = clamp(amax_group |w| / 7, min=1e-5); scale16 = scale.half();
     q = round(wg / scale16.float()).clamp(-7, 7) + 8; packed = pack_int4(q);
     scales = scale16.t()`` -> (packed uint8 [N, K/2], scales fp16 [K/128, N]).
-    ``qmin=-8`` with ``layout=LAYOUT_ADJACENT`` gives the BASELINE-config-1
+    ``qmin=-8`` with ``layout=LAYOUT_ADJACENT`` gives the benchmark-config-1
     variant ([-8, 7], low nibble = even k).
     """
     w = np.asarray(w).astype(np.float32)

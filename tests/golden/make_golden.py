@@ -106,7 +106,7 @@ def main():
         b = q.bias.float() if q.bias is not None else None
         int8[f"{name}/y32"] = torch.nn.functional.linear(
             x.float(), q.dequantized_weight(torch.float32), b).numpy()
-        # fp16-scale variant (BASELINE config 0 stores fp16 scales); the
+        # fp16-scale variant (benchmark config 0 stores fp16 scales); the
         # reference's oracle accepts it via scale.float().
         int8[f"{name}/y16_scale16"] = w8a16_reference(x, q.weight_q, q.scale.half(), q.bias).numpy()
     # edge rows: ties, zero row, extremes

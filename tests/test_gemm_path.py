@@ -85,7 +85,7 @@ def test_w8_gemm_forced(K, N, M):
 
 @pytest.mark.parametrize("wbits", [4, 8])
 def test_gemm_prefill_shapes(wbits):
-    """BASELINE config 3 shape class at a size the oracle finishes quickly."""
+    """benchmark config 3 shape class at a size the oracle finishes quickly."""
     for K, N, M in ((4096, 1024, 512), (2048, 4096, 256)):
         lin = make_linear(K, N, bias=False, std=0.02, seed=K ^ N)
         x = make_x(M, K, seed=M)

@@ -3,7 +3,7 @@
 Mirrors the reference's tests/test_w4a16_kernel.py (shapes incl. the awkward
 (384, 100), M in {1, 7, 16, 100, 300}, bias on/off, leading dims, error and
 byte bounds, half-step round trip) and adds the north-star tolerance against
-the CPU oracle, both nibble layouts, BASELINE configs 1/4 shapes, the device
+the CPU oracle, both nibble layouts, benchmark configs 1/4 shapes, the device
 nibble decoder / dequantizer / quantizer bit-exact against the oracle and
 the reference's fixtures (every nibble value, incl. 0 = -8), determinism,
 workspace hygiene and CUDA-graph capture.
@@ -88,7 +88,7 @@ def test_kernel_matches_dequantized_reference(K, N, M, bias):
 @pytest.mark.parametrize("M", [1, 8, 32])
 @pytest.mark.parametrize("layout", [LAYOUT_SPLIT_HALF, LAYOUT_ADJACENT])
 def test_baseline_config1(K, N, M, layout):
-    """x [M,K] N(0,1), W N(0,0.02), group-128 int4; the
+    """benchmark config 1: x [M,K] N(0,1), W N(0,0.02), group-128 int4; the
     reference format and the [-8,7] / low-nibble-even variant."""
     lin = make_linear(K, N, bias=False, std=0.02, seed=0)
     qmin = -7 if layout == LAYOUT_SPLIT_HALF else -8
@@ -156,7 +156,7 @@ def test_deterministic_pdl_and_workspace_clean(K, N, M):
 
 
 def test_lm_head_shape_config4():
-    """BASELINE config 4 lm_head 1536 -> 151936, M = 1 and 16 (one GPU)."""
+    """benchmark config 4 lm_head 1536 -> 151936, M = 1 and 16 (one GPU)."""
     K, N = 1536, 151936
     lin = make_linear(K, N, bias=False, std=0.02, seed=4)
     q = QuantizedLinearInt4.from_linear(lin)

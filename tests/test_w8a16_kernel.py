@@ -4,7 +4,7 @@ Mirrors the reference's tests/test_w8a16_kernel.py (same shapes, M values,
 bias on/off, 3-D input, quantization-error and byte bounds) and adds:
   * the north-star tolerance against the CPU oracle's fp32 result
     (max-abs <= 1e-2*|x|inf*|w|inf*sqrt(K)/64, rel-L2 <= 2e-3);
-  * the BASELINE config-0 case (fp16 scales);
+  * the benchmark config-0 case (fp16 scales);
   * ragged / tiny shapes, both kernel paths, determinism, workspace hygiene,
     PDL on/off, CUDA-graph capture, device quantizer/dequantizer bit-exact.
 """
@@ -94,7 +94,7 @@ def test_kernel_handles_3d_input():
 
 
 def test_baseline_config0_fp16_scales():
-    """BASELINE config 0: x [1,1536] N(0,1); W [8960,1536] N(0,0.02);
+    """benchmark config 0: x [1,1536] N(0,1); W [8960,1536] N(0,0.02);
     per-row int8 with fp16 scales."""
     lin = make_linear(1536, 8960, bias=False, std=0.02, seed=0)
     q = QuantizedLinearInt8.from_linear(lin)

@@ -35,14 +35,13 @@ def _args(x, q, out):
             _launch.ld(out, N))
 
 
-@pytest.mark.parametrize("M,N,K", [(8, 1536, 8960), (5, 1536, 8960), (8, 2048, 14336)])
+@pytest.mark.parametrize("M,N,K", [(8, 1536, 8960), (7, 1536, 8960), (5, 1024, 14336), (1, 512, 14336)])
 def test_static_scratch_matches_workspace_entry_point(M, N, K):
-    """Decode-kernel shapes with a K-split (the tensor-core kernel needs no
-    scratch: its splits reduce inside a cluster)."""
+    """Decode-kernel shapes whose plan splits K (3 to 5 ways on a 148-SM
+    B200, ql_gemv_plan) and so uses the scratch; the tensor-core kernel
+    needs none (its splits reduce inside a cluster)."""
     lib = _lib.load()
     need = lib.ql_w4a16_workspace_size(M, N, K)
-    if (M, N, K) != (8, 1536, 8960) and not 0 < need <= _lib.QL_STATIC_WS_BYTES:
-        pytest.skip("this device plans the shape without a K-split or beyond the static scratch")
     assert 0 < need <= _lib.QL_STATIC_WS_BYTES, "shape must exercise the split-K scratch"
     lin = make_linear(K, N, bias=True, std=0.02, seed=M + N)
     q = QuantizedLinearInt4.from_linear(lin).cuda()
@@ -70,18 +69,22 @@ def test_static_scratch_matches_workspace_entry_point(M, N, K):
 
 
 def test_static_scratch_rejects_oversized_plans():
+    """A decode-kernel shape (fewer than 8 rows) whose K-split needs more
+    scratch than the static array holds is refused before any launch.  The
+    candidates' plans need 2.5 to 6.6 MiB on a 148-SM B200 (ql_gemv_plan);
+    weights and scales are placeholders, since nothing may run."""
     lib = _lib.load()
-    # a decode-kernel shape whose split-K scratch exceeds the static array
-    # (the tensor-core kernel reduces its K-splits in a cluster: no scratch)
-    cands = [(M, 4096, 14336) for M in (47, 40, 33, 24)] + [(47, 8192, 28672)]
+    cands = [(7, 16384, 16384), (4, 8192, 57344), (7, 14336, 57344)]
     big = [c for c in cands if lib.ql_w4a16_workspace_size(*c) > _lib.QL_STATIC_WS_BYTES]
-    if not big:
-        pytest.skip("no candidate shape needs more than the static scratch on this device")
+    assert big, "on a B200 these shapes plan a K-split larger than the static scratch"
     M, N, K = big[0]
-    q = QuantizedLinearInt4.from_linear(make_linear(K, N, bias=False, std=0.02, seed=1)).cuda()
+    packed = torch.zeros((N, K // 2), dtype=torch.uint8, device="cuda")
+    scales = torch.ones((K // 128, N), dtype=torch.float16, device="cuda")
     x = make_x(M, K).cuda()
     o = torch.full((M, N), 7.0, dtype=torch.float16, device="cuda")
-    st = lib.ql_w4a16_linear_static_ws(*_args(x, q, o), 0, torch.cuda.current_stream().cuda_stream)
+    st = lib.ql_w4a16_linear_static_ws(x.data_ptr(), _lib.QL_DTYPE_F16, packed.data_ptr(), 0, scales.data_ptr(),
+                                       None, _lib.QL_DTYPE_F16, o.data_ptr(), M, N, K, K, K // 2, N, N, 0,
+                                       torch.cuda.current_stream().cuda_stream)
     assert st == _lib.QL_ERR_WORKSPACE
     assert b"workspace" in lib.ql_strerror(st)
     torch.cuda.synchronize()
