@@ -149,3 +149,60 @@ def test_sharded_nccl_two_gpus(case):
     assert len(res) == 2, (res, [p.exitcode for p in procs])
     for rank, ok, a, b in res:
         assert ok, (rank, a, b)
+
+
+def _gather_worker(rank, world, port, result_q):
+    """Back-to-back flagged all-gathers (5 MB of output each, over the 4 MB
+    tagged-line limit) with no host synchronisation between the calls: a
+    fast rank may already have published call e + 1 while a slow one still
+    waits for call e, which the wait must accept."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        from qlinear import _lib
+        from qlinear.p2p import PeerGather
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        M, N, calls = 64, 40960, 8
+        block = (N + world - 1) // world
+        lo, hi = rank * block, min(N, (rank + 1) * block)
+        gat = PeerGather(rank, world, max_m=M, n_cols=N)
+        outs = [torch.zeros(M, N, dtype=torch.float16, device="cuda") for _ in range(calls)]
+        dist.barrier()
+        for c, o in enumerate(outs):
+            o[:, lo:hi] = float(rank * 16 + c)
+            gat.gather(o, block)
+        torch.cuda.synchronize()
+        ok = _lib.device_error() == 0
+        for c, o in enumerate(outs):
+            want = torch.empty(M, N, dtype=torch.float16, device="cuda")
+            for q in range(world):
+                want[:, q * block:min(N, (q + 1) * block)] = float(q * 16 + c)
+            ok = ok and torch.equal(o, want)
+        gat.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        result_q.put((rank, bool(ok), None, None))
+    except Exception as e:
+        result_q.put((rank, False, repr(e)[:300], None))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_gather_back_to_back_flagged(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    res = sorted(q.get() for _ in range(q.qsize())) if not q.empty() else []
+    assert len(res) == world, (res, [p.exitcode for p in procs])
+    for rank, ok, a, b in res:
+        assert ok, (rank, a, b)
