@@ -331,11 +331,13 @@ def measure_config0(reps=20):
     x = torch.randn(1, K, generator=gen, device=dev).half()
     y = torch.empty(copies, N, dtype=torch.float16, device=dev)
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)
     peak, peak_kind = measured_peaks()
     res = {"shape": "x [1,1536] fp16, W int8 [8960,1536], per-row scale", "copies": copies,
            "reference_rtx4060": {"us": 58.4, "GBps": 235.9, "source": "benchmarks/results/stage7_kernel.json:91-99"}}
     for sdt, tag in ((torch.float32, "f32_scale"), (torch.float16, "f16_scale")):
         sc = [s.to(sdt) for _, s in layers]
+        torch.cuda.synchronize(dev)
         with torch.cuda.stream(stream):
             for c in range(copies):
                 w8a16_linear(x, layers[c][0], sc[c], out=y[c:c + 1])
@@ -521,6 +523,7 @@ def measure_decode_step(reps=20, warmup=3):
 
         for M in DECODE_MS:
             x = torch.randn(M, 1536, generator=gen, device=dev).half()
+            torch.cuda.synchronize(dev)          # weights and x are made on the default stream
             row = {}
             for fused, fn, nl in ((False, step_unfused, 7), (True, step_fused, 4)):
                 with torch.cuda.stream(stream):
@@ -735,6 +738,9 @@ def measure_sharded(world, rank, reps=5, ms=SHARDED_MS, layers=SHARDED_LAYERS):
             for M in ms:
                 gx = torch.Generator(device=dev).manual_seed(7000 + M)
                 x = torch.randn(M, K, generator=gx, device=dev).half()   # same on every rank
+                # weights, dequantized copy and x come from the default stream:
+                # all done before the side stream reads them
+                torch.cuda.synchronize(dev)
                 with torch.cuda.stream(stream):
                     # ---- parity (real layer)
                     ref32 = x.float() @ deq.t()
