@@ -79,6 +79,10 @@ extern "C" {
 #define QL_FLAG_FORCE_GEMV      0x4u
 /* Force the portable CUDA-core path (any shape / alignment).  Test hook.    */
 #define QL_FLAG_FORCE_GENERIC   0x8u
+/* Force the small-batch tensor-core kernel (tcgen05, decoded weights in
+ * TMEM; M <= 32, K % 128 == 0); QL_ERR_UNSUPPORTED where it cannot run.
+ * Test hook.                                                                */
+#define QL_FLAG_FORCE_TCDEC     0x10u
 
 /* ------------------------------------------------------------------ linear */
 /*
@@ -150,6 +154,14 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
  * clusters of that size the device holds at once (0 without a split)
  * (nfields >= 8).  No counterpart in the reference. */
 int ql_gemm_plan(int wbits, int layout, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields);
+
+/* The small-batch tensor-core kernel's plan for (wbits, M, N, K) on the
+ * current device: fields[0..6] = activation rows per tile (16 or 32),
+ * K-splits (= cluster size), 128-k blocks per split, ring stages, dynamic
+ * shared bytes, 128-row weight tiles, 1 if the dispatch sends this shape to
+ * it (nfields >= 7).  QL_ERR_UNSUPPORTED when the kernel cannot take the
+ * shape.  No counterpart in the reference. */
+int ql_tcdec_plan(int wbits, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields);
 
 /* ----------------------------------------------- no-allocation variant */
 /* Size of the fixed scratch array behind ql_w4a16_linear_static_ws. */

@@ -23,6 +23,7 @@
 #include "qxchg.cuh"
 #include "qgather.cuh"
 #include "qformat.cuh"
+#include "qdec.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
 
@@ -434,6 +435,7 @@ struct LinearArgs {
   cudaStream_t stream;
   int64_t swiglu_n = 0;   // > 0: fused gate+up, N = 2 * swiglu_n stacked weight rows
   const ql::xchg::Ctx* amax = nullptr;   // greedy head: argmax columns instead of outputs
+  bool no_tcdec = false;                 // keep the dispatch off the small-batch tensor-core kernel
 };
 
 int run_generic(const LinearArgs& a) {
@@ -826,6 +828,138 @@ int run_gemm(const LinearArgs& a, DeviceInfo* dev) {
   return run_gemm_layout<4, 1>(a, dev, g);
 }
 
+// ------------------------------------------- small-batch tensor-core kernel
+// qdec_kernel<WBITS, LAYOUT, BN> (csrc/qdec.cuh): 128 weight rows per CTA,
+// BN = 16 or 32 activation rows, the K range split over a thread-block
+// cluster when the tiles alone do not fill two CTAs per SM.
+struct DecPlan {
+  int bn = 0, ks = 1, kb_split = 0, stages = 0;
+  int64_t tiles = 0;
+  size_t smem = 0;
+};
+
+// Shapes the kernel takes: fast-path operands (checked by the caller), M <=
+// 32, K a multiple of 128 (a stage is one 128-k block of every row).
+bool dec_shape_ok(int wbits, int64_t M, int64_t N, int64_t K) {
+  (void)wbits;
+  return M >= 1 && M <= 32 && K >= 128 && K % 128 == 0 && N >= 1 && N <= INT_MAX && K <= INT_MAX;
+}
+
+// Optional override for tuning sweeps: QLINEAR_TCDEC_KS=<splits> (read like
+// QLINEAR_GEMV_PLAN: re-read on every call when set at the first call).
+int tcdec_override() {
+  static std::atomic<int> mode{-1};
+  int m = mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    m = std::getenv("QLINEAR_TCDEC_KS") ? 1 : 0;
+    mode.store(m, std::memory_order_relaxed);
+  }
+  if (m == 0) return 0;
+  const char* e = std::getenv("QLINEAR_TCDEC_KS");
+  int v = 0;
+  if (!e || std::sscanf(e, "%d", &v) != 1) return 0;
+  return v;
+}
+
+template <int WBITS, int BN>
+bool plan_dec_t(int64_t N, int64_t K, int sms, DecPlan* d) {
+  const int nkb = (int)(K / 128);
+  const int64_t tiles = cdiv(N, ql::dec::kRows);
+  const int kmax = std::min(ql::dec::kMaxSplits, nkb);
+  // K-split: enough CTAs for two per SM when the tiles alone are fewer; more
+  // splits when the activation tile would leave the ring shallower than 4
+  int ks0 = (int)std::max<int64_t>(1, std::min<int64_t>(2 * sms / tiles, kmax));
+  const int o = tcdec_override();
+  if (o > 0) ks0 = std::min(o, kmax);
+  bool found = false;
+  for (int ks = ks0; ks <= kmax; ++ks) {
+    const int kbs = (int)cdiv(nkb, ks);
+    const int ke = (int)cdiv(nkb, kbs);
+    // the deepest ring (up to 8 stages) that keeps two CTAs per SM
+    for (int S = std::min(ql::dec::kMaxStages, kbs); S >= std::min(2, kbs); --S) {
+      const size_t smem = ql::dec::smem_plan<WBITS, BN>(S, kbs, ke).total;
+      if (smem > kSmemTwoPerSm) continue;
+      if (!found || S > d->stages) {
+        d->bn = BN;
+        d->ks = ke;
+        d->kb_split = kbs;
+        d->stages = S;
+        d->tiles = tiles;
+        d->smem = smem;
+        found = true;
+      }
+      break;
+    }
+    if (found && (d->stages >= std::min(4, d->kb_split) || o > 0)) break;
+  }
+  return found;
+}
+
+bool plan_dec(int wbits, int64_t M, int64_t N, int64_t K, int sms, DecPlan* d) {
+  if (!dec_shape_ok(wbits, M, N, K)) return false;
+  if (wbits == 4) return M <= 16 ? plan_dec_t<4, 16>(N, K, sms, d) : plan_dec_t<4, 32>(N, K, sms, d);
+  return M <= 16 ? plan_dec_t<8, 16>(N, K, sms, d) : plan_dec_t<8, 32>(N, K, sms, d);
+}
+
+// Where the dispatch sends a plain linear to the small-batch tensor-core
+// kernel (see use_gemm for the rest).
+bool use_tcdec(int wbits, int64_t M, int64_t N, int64_t K) {
+  (void)N;
+  return wbits == 4 && M <= 16 && K % 128 == 0;
+}
+
+template <int WBITS, int LAYOUT, int BN>
+int launch_dec_t(const LinearArgs& a, const DecPlan& d, const CUtensorMap& tw, const ql::dec::Params& prm) {
+  auto kern = ql::dec::qdec_kernel<WBITS, LAYOUT, BN>;
+  static std::atomic<unsigned char> done[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!done[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOptin) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+      cudaGetLastError();
+      return QL_ERR_CUDA;
+    }
+    done[dev].store(1, std::memory_order_release);
+  }
+  dim3 grid((unsigned)d.tiles, 1, (unsigned)d.ks);
+  return launch_ex(kern, grid, dim3(ql::dec::kThreads), d.smem, a.stream, (a.flags & QL_FLAG_PDL) != 0, d.ks,
+                   tw, prm);
+}
+
+int run_dec(const LinearArgs& a, DeviceInfo* dev) {
+  DecPlan d;
+  if (!plan_dec(a.wbits, a.M, a.N, a.K, dev->sms, &d)) return QL_ERR_UNSUPPORTED;
+  if (d.tiles > INT_MAX) return QL_ERR_BAD_SHAPE;
+  const uint64_t kbytes = a.wbits == 4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
+  CUtensorMap tw;
+  int st = make_gemm_weight_map(&tw, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, a.wbits == 4 ? 64 : 128);
+  if (st != QL_OK) return st;
+  ql::dec::Params p;
+  p.x = static_cast<const __half*>(a.x);
+  p.scale = a.scale;
+  p.bias = a.bias;
+  p.out = static_cast<__half*>(a.out);
+  p.ldx = a.ldx;
+  p.lds = a.lds;
+  p.ldo = a.ldo;
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.nkb = (int)(a.K / 128);
+  p.kb_split = d.kb_split;
+  p.stages = d.stages;
+  p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
+  p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  p.err = dev->err_word;
+  if (a.wbits == 8) return d.bn == 16 ? launch_dec_t<8, 0, 16>(a, d, tw, p) : launch_dec_t<8, 0, 32>(a, d, tw, p);
+  if (a.layout == QL_W4_LAYOUT_SPLIT_HALF)
+    return d.bn == 16 ? launch_dec_t<4, 0, 16>(a, d, tw, p) : launch_dec_t<4, 0, 32>(a, d, tw, p);
+  return d.bn == 16 ? launch_dec_t<4, 1, 16>(a, d, tw, p) : launch_dec_t<4, 1, 32>(a, d, tw, p);
+}
+
 // Where the tensor-core GEMM replaces the decode kernel (measured on B200:
 // forced-path sweeps of both over M = 8..32 on the config-1 to 4 shapes):
 // from 24 batch rows always (the decode kernel re-decodes the weights for
@@ -904,7 +1038,15 @@ int run_linear(const LinearArgs& a) {
     if (!fast_ok || !gemm_ok(a)) return QL_ERR_UNSUPPORTED;
     return run_gemm(a, dev);
   }
+  if (a.flags & QL_FLAG_FORCE_TCDEC) {
+    if (!fast_ok || !dec_shape_ok(a.wbits, a.M, a.N, a.K) || !gemm_ok(a)) return QL_ERR_UNSUPPORTED;
+    return run_dec(a, dev);
+  }
   if ((a.flags & QL_FLAG_FORCE_GENERIC) || !fast_ok) return run_generic(a);
+  if (!(a.flags & QL_FLAG_FORCE_GEMV) && !a.no_tcdec && use_tcdec(a.wbits, a.M, a.N, a.K) && gemm_ok(a)) {
+    const int st = run_dec(a, dev);
+    if (st != QL_ERR_UNSUPPORTED) return st;
+  }
   if (!(a.flags & QL_FLAG_FORCE_GEMV) && use_gemm(a.wbits, a.M, a.N, a.K) && gemm_ok(a)) return run_gemm(a, dev);
   return run_gemv(a, dev);
 }
@@ -1141,6 +1283,20 @@ int ql_gemv_plan(int wbits, int64_t M, int64_t N, int64_t K, size_t workspace_by
   return QL_OK;
 }
 size_t ql_w4a16_workspace_size(int64_t M, int64_t N, int64_t K) { return workspace_size(4, M, N, K); }
+
+int ql_tcdec_plan(int wbits, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields) {
+  if (!fields || nfields < 7) return QL_ERR_NULL_POINTER;
+  if ((wbits != 4 && wbits != 8) || M <= 0 || N <= 0 || K <= 0) return QL_ERR_BAD_SHAPE;
+  int st;
+  DeviceInfo* dev = current_device(&st);
+  const int sms = dev ? dev->sms : 148;   // without a device: the B200 SM count
+  DecPlan d;
+  if (!plan_dec(wbits, M, N, K, sms, &d)) return QL_ERR_UNSUPPORTED;
+  const int64_t v[7] = {d.bn, d.ks, d.kb_split, d.stages, (int64_t)d.smem, d.tiles,
+                        use_tcdec(wbits, M, N, K) ? 1 : 0};
+  for (int i = 0; i < 7; ++i) fields[i] = v[i];
+  return QL_OK;
+}
 
 int ql_gemm_plan(int wbits, int layout, int64_t M, int64_t N, int64_t K, int64_t* fields, int nfields) {
   if (!fields || nfields < 8) return QL_ERR_NULL_POINTER;
@@ -1450,6 +1606,7 @@ int ql_w4a16_linear_static_ws(const void* x, int x_dtype, const void* w_packed, 
   if (w.status != QL_OK) return w.status;
   LinearArgs a{4, x, w_packed, layout, scales, QL_DTYPE_F16, bias, bias_dtype, out, M, N, K, ldx, ldw, lds,
                ldo, w.ptr, (size_t)QL_STATIC_WS_BYTES, flags, static_cast<cudaStream_t>(stream)};
+  a.no_tcdec = true;   // the decode kernel with its split-K scratch, as the size check above assumes
   return run_linear(a);
 }
 

@@ -46,6 +46,7 @@ QL_FLAG_PDL = 0x1
 QL_FLAG_FORCE_GEMM = 0x2
 QL_FLAG_FORCE_GEMV = 0x4
 QL_FLAG_FORCE_GENERIC = 0x8
+QL_FLAG_FORCE_TCDEC = 0x10
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -71,6 +72,7 @@ SIGNATURES = {
     "ql_w4a16_workspace_size": (_sz, [_i64, _i64, _i64]),
     "ql_gemv_plan": (_int, [_int, _i64, _i64, _i64, _sz, ctypes.POINTER(_i64), _int]),
     "ql_gemm_plan": (_int, [_int, _int, _i64, _i64, _i64, ctypes.POINTER(_i64), _int]),
+    "ql_tcdec_plan": (_int, [_int, _i64, _i64, _i64, ctypes.POINTER(_i64), _int]),
     "ql_w8a16_dequantize": (_int, [_vp, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "ql_w4a16_dequantize": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ql_w4a16_unpack": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
@@ -162,6 +164,21 @@ def gemm_plan(wbits: int, M: int, N: int, K: int, layout: int = QL_W4_LAYOUT_SPL
     buf = (_i64 * 8)()
     check(load().ql_gemm_plan(wbits, layout, M, N, K, buf, 8))
     return dict(zip(GEMM_PLAN_FIELDS, list(buf)))
+
+
+TCDEC_PLAN_FIELDS = ("rows_per_tile", "k_splits", "blocks_per_split", "stages", "smem_bytes", "tiles",
+                     "dispatched")
+
+
+def tcdec_plan(wbits: int, M: int, N: int, K: int) -> dict | None:
+    """The small-batch tensor-core kernel's plan for a shape (see
+    ql_tcdec_plan); None where the kernel cannot take it."""
+    buf = (_i64 * 7)()
+    st = load().ql_tcdec_plan(wbits, M, N, K, buf, 7)
+    if st == QL_ERR_UNSUPPORTED:
+        return None
+    check(st)
+    return dict(zip(TCDEC_PLAN_FIELDS, list(buf)))
 
 
 def version() -> tuple[int, int, int]:
