@@ -1157,7 +1157,8 @@ def run_profile_one(args):
         # one kernel family forced through the C ABI (its split-K workspace included)
         from qlinear import _lib
         lib = _lib.load()
-        flag = (_lib.QL_FLAG_FORCE_GEMM if args.path == "gemm" else _lib.QL_FLAG_FORCE_GEMV) | _lib.QL_FLAG_PDL
+        flag = {"gemm": _lib.QL_FLAG_FORCE_GEMM, "gemv": _lib.QL_FLAG_FORCE_GEMV,
+                "tcdec": _lib.QL_FLAG_FORCE_TCDEC}[args.path] | _lib.QL_FLAG_PDL
         out = torch.empty(M, N, dtype=torch.float16, device=dev)
         ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
@@ -1188,8 +1189,8 @@ def main():
     ap.add_argument("--workload", choices=("config1", "decode_step", "prefill", "sharded"), default="config1")
     ap.add_argument("--profile-one", default=None, metavar="WBITS,M,K,N",
                     help="a few eager launches of one layer shape (small case for ncu)")
-    ap.add_argument("--path", choices=("auto", "gemv", "gemm"), default="auto",
-                    help="with --profile-one: force the decode or the tensor-core kernel")
+    ap.add_argument("--path", choices=("auto", "gemv", "gemm", "tcdec"), default="auto",
+                    help="with --profile-one: force the decode, prefill or small-batch tensor-core kernel")
     args = ap.parse_args()
     if args.profile_one:
         return run_profile_one(args)

@@ -419,18 +419,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     griddep_launch_dependents();
 
-    // ---- blocks of this set: decode ahead, epilogue in order
+    // ---- blocks of this set: epilogue in order, then decode ahead.  The
+    // epilogue of block g frees this set's D columns for the MMAs of block
+    // g + 2, so it goes first; the decode runs up to kNA blocks ahead of the
+    // MMAs (each A slot is reused once the MMAs of the block kNA earlier are
+    // done).
     float acc[BN];
     #pragma unroll
     for (int m = 0; m < BN; ++m) acc[m] = 0.f;
     const int M = p.M;
     int kth = 0;                                   // blocks of this set finished
     for (int g = set; ok && g < G; g += 2, ++kth) {
-      if (gnext < G) {
-        ok = decode(gnext);
-        gnext += 2;
-        if (!ok) break;
-      }
       if (WBITS == 4) {
         if (!__all_sync(0xffffffffu, mbar_wait(dfull + set, kth & 1, p.err, kDevErrMmaWait, abort))) {
           ok = false;
@@ -456,7 +455,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(dfree + set);
       }
+      if (gnext < G) {
+        ok = decode(gnext);
+        gnext += 2;
+      }
     }
+    // int8 has no per-block epilogue: the loop above only decodes; finish
+    // the decode of this set's remaining blocks
+    for (; ok && gnext < G; gnext += 2) ok = decode(gnext);
     if (!ok) *abort = 1;
 
     // ---- this CTA's partial of row r: set 1 hands its sums to set 0

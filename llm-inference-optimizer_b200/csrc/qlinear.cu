@@ -862,7 +862,7 @@ int tcdec_override() {
 }
 
 template <int WBITS, int BN>
-bool plan_dec_t(int64_t N, int64_t K, int sms, DecPlan* d) {
+bool plan_dec_budget(int64_t N, int64_t K, int sms, size_t budget, DecPlan* d) {
   const int nkb = (int)(K / 128);
   const int64_t tiles = cdiv(N, ql::dec::kRows);
   const int kmax = std::min(ql::dec::kMaxSplits, nkb);
@@ -878,7 +878,7 @@ bool plan_dec_t(int64_t N, int64_t K, int sms, DecPlan* d) {
     // the deepest ring (up to 8 stages) that keeps two CTAs per SM
     for (int S = std::min(ql::dec::kMaxStages, kbs); S >= std::min(2, kbs); --S) {
       const size_t smem = ql::dec::smem_plan<WBITS, BN>(S, kbs, ke).total;
-      if (smem > kSmemTwoPerSm) continue;
+      if (smem > budget) continue;
       if (!found || S > d->stages) {
         d->bn = BN;
         d->ks = ke;
@@ -895,6 +895,13 @@ bool plan_dec_t(int64_t N, int64_t K, int sms, DecPlan* d) {
   return found;
 }
 
+// Two CTAs per SM where the activation tile allows, else one.
+template <int WBITS, int BN>
+bool plan_dec_t(int64_t N, int64_t K, int sms, DecPlan* d) {
+  return plan_dec_budget<WBITS, BN>(N, K, sms, kSmemTwoPerSm, d) ||
+         plan_dec_budget<WBITS, BN>(N, K, sms, kSmemOptin, d);
+}
+
 bool plan_dec(int wbits, int64_t M, int64_t N, int64_t K, int sms, DecPlan* d) {
   if (!dec_shape_ok(wbits, M, N, K)) return false;
   if (wbits == 4) return M <= 16 ? plan_dec_t<4, 16>(N, K, sms, d) : plan_dec_t<4, 32>(N, K, sms, d);
@@ -902,10 +909,20 @@ bool plan_dec(int wbits, int64_t M, int64_t N, int64_t K, int sms, DecPlan* d) {
 }
 
 // Where the dispatch sends a plain linear to the small-batch tensor-core
-// kernel (see use_gemm for the rest).
+// kernel: nowhere, measured.  On B200 one tcgen05.mma with the weights as
+// the TMEM A operand (M = 128, K = 16) takes about 125 SM cycles whatever N
+// is (timestamped inside the kernel: 8 K-steps of a 128-k block take ~1000
+// cycles, the same with the steps spread over four independent
+// accumulators), i.e. ~16 fp16 weights per SM cycle: ~2 TB/s of int4 at any
+// batch size up to 32, below the mma.sync decode kernel (3.3 TB/s on the
+// 1536 -> 151936 lm_head at M = 1) and, from 24 rows, the prefill GEMM.  The
+// kernel stays reachable with QL_FLAG_FORCE_TCDEC.
 bool use_tcdec(int wbits, int64_t M, int64_t N, int64_t K) {
+  (void)wbits;
+  (void)M;
   (void)N;
-  return wbits == 4 && M <= 16 && K % 128 == 0;
+  (void)K;
+  return false;
 }
 
 template <int WBITS, int LAYOUT, int BN>

@@ -170,3 +170,44 @@ def test_exchange_peer_wait_is_bounded():
     finally:
         for b in bufs:
             lib.ql_xchg_free(b)
+
+
+@pytest.mark.parametrize("wbits", [4, 8])
+@pytest.mark.parametrize("K,N", [(1536, 151936), (4096, 128256)])
+def test_greedy_head_against_oracle_on_lm_heads(wbits, K, N):
+    """The greedy head (one launch: the decode kernel makes the keys and its
+    last CTA combines them) on the real lm_head shapes, against the CPU
+    oracle's fp32 product: every chosen column holds its row's maximum of
+    the oracle's logits to within the north-star bound (two columns closer
+    than that are a tie either path may break either way), and equals the
+    argmax of the same plan's fp16 logits exactly."""
+    import numpy as np
+    from oracle import qlinear_oracle as orc
+    from qlinear.p2p import PeerExchange
+    from qlinear.quantization.int8 import QuantizedLinearInt8
+    g = torch.Generator(device="cuda").manual_seed(K + wbits)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).half()
+    lin = torch.nn.Linear(K, N, bias=False, device="cuda", dtype=torch.float16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    del w
+    q = QuantizedLinearInt4.from_linear(lin) if wbits == 4 else QuantizedLinearInt8.from_linear(lin)
+    del lin
+    M = 4
+    x = torch.randn(M, K, generator=g, device="cuda").half()
+    px = PeerExchange(0, 1, max_m=8)
+    ids = px.linear_argmax(x, q, 0)
+    assert ids is not None, "a one-rank greedy head takes these shapes in one launch"
+    same_plan = torch.argmax(linear_unsplit(q, x), dim=-1)
+    torch.cuda.synchronize()
+    px.close()
+    assert torch.equal(ids, same_plan)
+    if wbits == 4:
+        deq = orc.dequantize_int4(q.weight_packed.cpu().numpy(), q.scales.cpu().numpy())
+    else:
+        deq = orc.dequantize_int8(q.weight_q.cpu().numpy(), q.scale.cpu().numpy())
+    xn = x.cpu().numpy()
+    y32 = orc.linear_f32(xn, deq, None)
+    bound = orc.parity_bounds(xn, deq)[0]
+    picked = y32[np.arange(M), ids.cpu().numpy()]
+    assert (picked >= y32.max(axis=1) - 2 * bound).all(), (picked, y32.max(axis=1), bound)

@@ -99,6 +99,41 @@ def test_gemm_prefill_shapes(wbits):
         assert_parity(out, y32, x.numpy(), deq, f"prefill w{wbits} K{K} N{N} M{M}")
 
 
+@pytest.mark.parametrize("wbits", [4, 8])
+@pytest.mark.parametrize("M,K,N", [(2048, 14336, 4096), (8192, 4096, 14336), (8192, 14336, 4096),
+                                   (2048, 1536, 8960)])
+def test_prefill_full_size(M, K, N, wbits):
+    """Benchmark config 3 at its real sizes (the 192-row int8 tile from M =
+    1024, multi-wave grids): weights quantized on the device, the whole
+    product on the GPU through the default dispatch, the oracle on row and
+    column slices at both ends (cheap on the CPU), bit-identical on a second
+    run."""
+    g = torch.Generator(device="cuda").manual_seed(M + K + N + wbits)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).half()
+    lin = torch.nn.Linear(K, N, bias=False, device="cuda", dtype=torch.float16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    del w
+    q = QuantizedLinearInt4.from_linear(lin) if wbits == 4 else QuantizedLinearInt8.from_linear(lin)
+    del lin
+    x = torch.randn(M, K, generator=g, device="cuda").half()
+    y = q(x)
+    y2 = q(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    assert bool(torch.isfinite(y).all())
+    rows = np.r_[0:48, M - 48:M]
+    xs = x[rows].cpu().numpy()
+    for a, b in ((0, 384), (N - 384, N)):
+        if wbits == 4:
+            deq = orc.dequantize_int4(q.weight_packed[a:b].cpu().numpy(), q.scales[:, a:b].cpu().numpy())
+        else:
+            deq = orc.dequantize_int8(q.weight_q[a:b].cpu().numpy(), q.scale[a:b].cpu().numpy())
+        y32 = orc.linear_f32(xs, deq, None)
+        assert_parity(y[rows][:, a:b], y32, xs, deq, f"prefill w{wbits} M{M} K{K} N{N} cols {a}:{b}")
+    assert _lib.device_error() == 0
+
+
 def test_gemm_unsupported_shape_is_reported():
     """int8 with K % 128 != 0 cannot take the tensor-core path; forcing it is
     an error status, not a fallback."""
