@@ -54,6 +54,7 @@ namespace gather {
 
 constexpr int kMaxRanks = 8;
 constexpr long long kLineMaxPayload = 4ll << 20;   // bytes of output [M, N] fp16 sent as tagged lines
+constexpr int kBatch = 4;    // loads a thread keeps in flight before its stores (push and copy loops)
 
 struct Layout {
   size_t flags, state, data, lines, total;
@@ -140,19 +141,32 @@ __device__ __forceinline__ void gather_lines(const Params& p, const Layout& L, u
   {
     const long long wu = shard_width(p, p.rank) / 4;
     const long long units = (long long)p.M * p.groups * wu;
-    for (long long i = tid; i < units; i += nthr) {
-      int m;
-      long long j, col;
-      locate(p.groups, ngu, bu, p.rank, wu, i, m, j, col);
-      __half* o = p.out + (long long)m * p.ldo + col * 4;
-      const uint2 v = p.src ? *reinterpret_cast<const uint2*>(p.src + (long long)m * p.lds + j * 4)
-                            : *reinterpret_cast<const uint2*>(o);
-      if (p.src) *reinterpret_cast<uint2*>(o) = v;
-      const unsigned long long tag = (unsigned long long)e << 32;
-      const unsigned long long wa = tag | v.x, wb = tag | v.y;
-      for (int k = 1; k < p.world; ++k) {
-        const int q = (p.rank + k) % p.world;
-        st_line(reinterpret_cast<uint4*>(p.peer[q] + L.lines) + bank + (long long)m * ldl + col, wa, wb);
+    const unsigned long long tag = (unsigned long long)e << 32;
+    for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+      // kBatch loads in flight per thread before any store
+      uint2 v[kBatch];
+      int mm[kBatch];
+      long long cc[kBatch];
+      #pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const long long i = i0 + u * nthr;
+        mm[u] = -1;
+        if (i < units) {
+          long long j;
+          locate(p.groups, ngu, bu, p.rank, wu, i, mm[u], j, cc[u]);
+          v[u] = p.src ? *reinterpret_cast<const uint2*>(p.src + (long long)mm[u] * p.lds + j * 4)
+                       : *reinterpret_cast<const uint2*>(p.out + (long long)mm[u] * p.ldo + cc[u] * 4);
+        }
+      }
+      #pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (mm[u] < 0) continue;
+        if (p.src) *reinterpret_cast<uint2*>(p.out + (long long)mm[u] * p.ldo + cc[u] * 4) = v[u];
+        const unsigned long long wa = tag | v[u].x, wb = tag | v[u].y;
+        for (int k = 1; k < p.world; ++k) {
+          const int q = (p.rank + k) % p.world;
+          st_line(reinterpret_cast<uint4*>(p.peer[q] + L.lines) + bank + (long long)mm[u] * ldl + cc[u], wa, wb);
+        }
       }
     }
   }
@@ -167,27 +181,40 @@ __device__ __forceinline__ void gather_lines(const Params& p, const Layout& L, u
     const int q = (p.rank + k) % p.world;
     const long long wu = shard_width(p, q) / 4;
     const long long units = (long long)p.M * p.groups * wu;
-    for (long long i = tid; i < units; i += nthr) {
-      int m;
-      long long j, col;
-      locate(p.groups, ngu, bu, q, wu, i, m, j, col);
-      const uint4* src = lines + (long long)m * ldl + col;
-      unsigned long long wa, wb;
-      ld_line(src, wa, wb);
-      if (((unsigned)(wa >> 32) != e || (unsigned)(wb >> 32) != e) && waiting) {
-        const long long t0 = clock64();
-        for (;;) {
-          ld_line(src, wa, wb);
-          if ((unsigned)(wa >> 32) == e && (unsigned)(wb >> 32) == e) break;
-          if (clock64() - t0 > kWaitBudgetCycles) {
-            atomicCAS(p.err, 0u, kDevErrPeerWait);
-            waiting = false;
-            break;
-          }
-          __nanosleep(32);
+    for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+      unsigned long long wa[kBatch], wb[kBatch];
+      int mm[kBatch];
+      long long cc[kBatch];
+      #pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const long long i = i0 + u * nthr;
+        mm[u] = -1;
+        if (i < units) {
+          long long j;
+          locate(p.groups, ngu, bu, q, wu, i, mm[u], j, cc[u]);
+          ld_line(lines + (long long)mm[u] * ldl + cc[u], wa[u], wb[u]);
         }
       }
-      *reinterpret_cast<uint2*>(p.out + (long long)m * p.ldo + col * 4) = make_uint2((unsigned)wa, (unsigned)wb);
+      #pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (mm[u] < 0) continue;
+        const uint4* src = lines + (long long)mm[u] * ldl + cc[u];
+        if (((unsigned)(wa[u] >> 32) != e || (unsigned)(wb[u] >> 32) != e) && waiting) {
+          const long long t0 = clock64();
+          for (;;) {
+            ld_line(src, wa[u], wb[u]);
+            if ((unsigned)(wa[u] >> 32) == e && (unsigned)(wb[u] >> 32) == e) break;
+            if (clock64() - t0 > kWaitBudgetCycles) {
+              atomicCAS(p.err, 0u, kDevErrPeerWait);
+              waiting = false;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        *reinterpret_cast<uint2*>(p.out + (long long)mm[u] * p.ldo + cc[u] * 4) =
+            make_uint2((unsigned)wa[u], (unsigned)wb[u]);
+      }
     }
   }
 }
@@ -219,21 +246,39 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
   {
     const long long wu = shard_width(p, p.rank) / vw;
     const long long units = (long long)p.M * p.groups * wu;
-    for (long long i = tid; i < units; i += nthr) {
-      int m;
-      long long j, col;
-      locate(p.groups, ngu, bu, p.rank, wu, i, m, j, col);
-      col *= vw;
-      if (p.vec) {
-        const uint4 v = p.src ? *reinterpret_cast<const uint4*>(p.src + (long long)m * p.lds + j * 8)
-                              : __ldcg(reinterpret_cast<const uint4*>(p.out + (long long)m * p.ldo + col));
-        if (p.src) *reinterpret_cast<uint4*>(p.out + (long long)m * p.ldo + col) = v;
-        for (int k = 1; k < p.world; ++k) {
-          const int q = (p.rank + k) % p.world;
-          __half* dst = reinterpret_cast<__half*>(p.peer[q] + L.data) + bank + (long long)m * L.ldb + col;
-          *reinterpret_cast<uint4*>(dst) = v;
+    if (p.vec) {
+      for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+        uint4 v[kBatch];
+        int mm[kBatch];
+        long long cc[kBatch];
+        #pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const long long i = i0 + u * nthr;
+          mm[u] = -1;
+          if (i < units) {
+            long long j;
+            locate(p.groups, ngu, bu, p.rank, wu, i, mm[u], j, cc[u]);
+            cc[u] *= vw;
+            v[u] = p.src ? *reinterpret_cast<const uint4*>(p.src + (long long)mm[u] * p.lds + j * 8)
+                         : __ldcg(reinterpret_cast<const uint4*>(p.out + (long long)mm[u] * p.ldo + cc[u]));
+          }
         }
-      } else {
+        #pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (mm[u] < 0) continue;
+          if (p.src) *reinterpret_cast<uint4*>(p.out + (long long)mm[u] * p.ldo + cc[u]) = v[u];
+          for (int k = 1; k < p.world; ++k) {
+            const int q = (p.rank + k) % p.world;
+            __half* dst = reinterpret_cast<__half*>(p.peer[q] + L.data) + bank + (long long)mm[u] * L.ldb + cc[u];
+            *reinterpret_cast<uint4*>(dst) = v[u];
+          }
+        }
+      }
+    } else {
+      for (long long i = tid; i < units; i += nthr) {
+        int m;
+        long long j, col;
+        locate(p.groups, ngu, bu, p.rank, wu, i, m, j, col);
         const __half v = p.src ? p.src[(long long)m * p.lds + j] : p.out[(long long)m * p.ldo + col];
         if (p.src) p.out[(long long)m * p.ldo + col] = v;
         for (int k = 1; k < p.world; ++k) {
@@ -281,15 +326,32 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
     __syncthreads();
     const long long wu = shard_width(p, q) / vw;
     const long long units = (long long)p.M * p.groups * wu;
-    for (long long i = tid; i < units; i += nthr) {
-      int m;
-      long long j, col;
-      locate(p.groups, ngu, bu, q, wu, i, m, j, col);
-      col *= vw;
-      if (p.vec) {
-        *reinterpret_cast<uint4*>(p.out + (long long)m * p.ldo + col) =
-            __ldcg(reinterpret_cast<const uint4*>(data + (long long)m * L.ldb + col));
-      } else {
+    if (p.vec) {
+      for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+        uint4 v[kBatch];
+        int mm[kBatch];
+        long long cc[kBatch];
+        #pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const long long i = i0 + u * nthr;
+          mm[u] = -1;
+          if (i < units) {
+            long long j;
+            locate(p.groups, ngu, bu, q, wu, i, mm[u], j, cc[u]);
+            cc[u] *= vw;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(data + (long long)mm[u] * L.ldb + cc[u]));
+          }
+        }
+        #pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (mm[u] >= 0) *reinterpret_cast<uint4*>(p.out + (long long)mm[u] * p.ldo + cc[u]) = v[u];
+      }
+    } else {
+      for (long long i = tid; i < units; i += nthr) {
+        int m;
+        long long j, col;
+        locate(p.groups, ngu, bu, q, wu, i, m, j, col);
+        col *= vw;
         p.out[(long long)m * p.ldo + col] = __ldcg(data + (long long)m * L.ldb + col);
       }
     }
