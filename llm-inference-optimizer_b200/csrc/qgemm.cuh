@@ -22,8 +22,17 @@
 //   * warp 1 (one thread): issues tcgen05.mma.cta_group::1.kind::f16
 //     (A from TMEM, B from shared memory by descriptor, fp32 accumulator
 //     in TMEM) and tcgen05.commit's the stage back to producer/dequant.
+//     64-row activation tiles add a second issuer (warp 10) that takes the
+//     odd stages into a second accumulator: measured on B200, a thread
+//     issuing K = 16 MMAs back to back gets one through every ~57 cycles or
+//     more whatever N is, while two issuers together reach ~40 (N = 16) to
+//     ~64 (N = 128, the dense peak).  With it the 64-row tiles of the large
+//     layers run 6-11 % (int4) and up to 35 % (int8) faster; the 16- and
+//     32-row tiles, bound elsewhere, are unchanged or slower with it and
+//     keep one issuer.  The epilogue adds the two accumulators in a fixed
+//     order.
 //   * epilogue (warps 2-9, each half of the activation columns): tcgen05.ld
-//     of the accumulator, int8 row scale and bias in fp32, fp16 store (32
+//     of the accumulator(s), int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
 //   * split-K (grids with fewer tiles than SMs): the K-splits of one tile
 //     are one thread-block cluster (cluster dims 1 x 1 x splits, at most 16);
@@ -47,7 +56,9 @@ namespace gemm {
 
 constexpr int kTileN = 128;     // weight rows per CTA = UMMA M
 constexpr int kBK = 128;        // k per stage = 8 MMAs of K=16
-constexpr int kThreads = 320;   // 10 warps: producer, MMA, 8 dequant/epilogue
+// Warps: 0 producer, 1 MMA issuer, 2-9 dequant/epilogue, and (64-row
+// activation tiles) 10 the second MMA issuer; Layout::kThreads.
+constexpr int kIssuer1Warp = 10;
 constexpr int kASlots = 2;      // A (dequantized weight) stages in TMEM
 
 struct Params {
@@ -75,6 +86,9 @@ struct Layout {
   static constexpr int kStage = kXStage + kWStage;  // multiple of 1024
   static constexpr uint32_t kTmemCols = BN + kASlots * 64 <= 256 ? 256 : 512;
   static constexpr uint32_t kACol = BN <= 128 ? 128 : 256;  // first A column
+  // second MMA issuer and accumulator (columns [BN, 2 BN), below kACol)
+  static constexpr bool kTwoIssuers = BN == 64;
+  static constexpr int kThreads = kTwoIssuers ? 352 : 320;
   static constexpr uint32_t kTx = kStage;
   // Split-K reduction: narrow tiles push their partial into the members'
   // receive buffers (one cluster barrier); wide tiles park it in the
@@ -156,6 +170,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 8 consecutive fp32 accumulator columns of this thread's TMEM lane, not
+// waited (tmem_ld_wait before use).
+__device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
 // 8 consecutive fp32 accumulator columns of this thread's TMEM lane, waited.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -226,7 +248,7 @@ __device__ __forceinline__ void reduce_slice(const Params& p, uint32_t base, int
 }
 
 template <int WBITS, int LAYOUT, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                  const Params p) {
   using L = Layout<WBITS, BN>;
@@ -248,6 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // this CTA's K-split: stages [kbeg, kbeg + nk)
   const int kbeg = blockIdx.z * p.nk_split;
   const int nk = min(p.nk - kbeg, p.nk_split);
+  // MMA issuers: issuer q takes stages q, q + nissuers, ... into the
+  // accumulator at TMEM column q * BN
+  const int nissuers = (L::kTwoIssuers && nk > 1) ? 2 : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -259,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(afull + a, 8);
       mbar_init(afree + a, 1);
     }
-    mbar_init(dfull, 1);
+    mbar_init(dfull, nissuers);
     *abort = 0;
     fence_barrier_init();
   }
@@ -316,11 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(full + s, (last / S) & 1, p.err, kDevErrFullWait);
       }
     }
-  } else if (warp == 1) {
-    // --------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || warp == kIssuer1Warp) {
+    // -------------------------------------------------------- MMA issuers
+    const int q = warp == 1 ? 0 : 1;
+    if (lane == 0 && q < nissuers) {
       const uint32_t idesc = idesc_f16<BN>();
-      for (int i = 0; i < nk; ++i) {
+      const uint32_t d_tmem = tmem + (uint32_t)(q * BN);
+      for (int i = q; i < nk; i += nissuers) {
         const int s = i % S, a = i % kASlots;
         if (!mbar_wait(full + s, (i / S) & 1, p.err, kDevErrMmaWait, abort) ||
             !mbar_wait(afull + a, (i / kASlots) & 1, p.err, kDevErrMmaWait, abort)) {
@@ -333,13 +360,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint64_t bd = desc_sw128(xs + (uint32_t)((j >> 2) * L::kXAtom + (j & 3) * 32));
-          tc_mma_ts(tmem, a_tmem + 8u * j, bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+          tc_mma_ts(d_tmem, a_tmem + 8u * j, bd, idesc, (i > q || j > 0) ? 1u : 0u);
         }
         tc_commit(xfree + s);
         tc_commit(afree + a);
       }
-      // dfull tracks every MMA issued above; waiting for it here means no
-      // MMA is in flight when the TMEM is released, on the error path too
+      // dfull tracks every MMA issued above (one arrival per issuer);
+      // waiting for it here means no MMA is in flight when the TMEM is
+      // released, on the error path too
       tc_commit(dfull);
       mbar_wait(dfull, 0, p.err, kDevErrMmaWait);
     }
@@ -451,6 +479,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // epilogue: this warp stores activation columns [half*BN/2, (half+1)*BN/2)
     mbar_wait(dfull, 0, p.err, kDevErrMmaWait);
     tc_fence_after();
+    // 8 accumulator columns of this lane: D0, or D0 + D1 (fixed order)
+    auto ld_acc = [&](uint32_t taddr, uint32_t (&v)[8]) {
+      if (nissuers == 2) {
+        uint32_t u[8];
+        tmem_ld8_async(taddr, v);
+        tmem_ld8_async(taddr + (uint32_t)BN, u);
+        tmem_ld_wait();
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
+      } else {
+        tmem_ld8(taddr, v);
+      }
+    };
     float sc8 = 1.f, bv = 0.f;
     if (n < p.N) {
       if (WBITS == 8)
@@ -465,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       #pragma unroll 1
       for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
         uint32_t v[8];
-        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        ld_acc(tmem + lane_base + (uint32_t)c0, v);
         if (n < p.N) {
           #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -487,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       #pragma unroll 1
       for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
         uint32_t v[8];
-        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        ld_acc(tmem + lane_base + (uint32_t)c0, v);
         #pragma unroll
         for (int j = 0; j < 8; ++j) {
           st_dsmem_f32(dsmem_addr(recv + (uint32_t)(me * sz + off) * 4u, (uint32_t)owner), __uint_as_float(v[j]));
@@ -507,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       #pragma unroll 1
       for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
         uint32_t v[8];
-        tmem_ld8(tmem + lane_base + (uint32_t)c0, v);
+        ld_acc(tmem + lane_base + (uint32_t)c0, v);
         #pragma unroll
         for (int j = 0; j < 8; ++j) part[(c0 + j) * kTileN + r] = __uint_as_float(v[j]);
       }
@@ -517,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (gridDim.z > 1 && L::kPush) {
     // ------------------------------------------ cluster reduction (push)
     cluster_sync_all();                 // every member's slices are in this CTA's receive buffer
-    if (warp >= 2) {
+    if (warp >= 2 && warp < kIssuer1Warp) {
       const int ks = (int)gridDim.z;
       constexpr int E = BN * kTileN;
       const int sz = (E + ks - 1) / ks;
@@ -545,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (gridDim.z > 1) {
     // ------------------------------------------ cluster reduction (pull)
     cluster_sync_all();                 // every member's partial is in its shared memory
-    if (warp >= 2) {
+    if (warp >= 2 && warp < kIssuer1Warp) {
       const int ks = (int)gridDim.z;
       const uint32_t me = cluster_rank();
       constexpr int E = BN * kTileN;

@@ -596,7 +596,7 @@ int max_active_clusters(int cz, size_t smem, bool cacheable) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, (unsigned)cz);
-  cfg.blockDim = dim3(ql::gemm::kThreads);
+  cfg.blockDim = dim3(ql::gemm::Layout<WBITS, BN>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -638,7 +638,7 @@ int ctas_per_sm(size_t smem) {
     return 1;
   }
   int n = (int)((size_t)smem_sm / (smem + (size_t)reserved));
-  n = std::min(n, 65536 / std::max(1, fa.numRegs * ql::gemm::kThreads));
+  n = std::min(n, 65536 / std::max(1, fa.numRegs * ql::gemm::Layout<WBITS, BN>::kThreads));
   n = std::min(n, (int)(512 / L::kTmemCols));
   n = std::max(1, n);
   if (dev < kMaxDevices) cache[dev].store(n, std::memory_order_relaxed);
@@ -732,7 +732,7 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
   dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)g.ks);
   if (grid.y > 65535 || grid.z > 65535) return QL_ERR_BAD_SHAPE;
   const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
-  st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem, a.stream, pdl,
+  st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::Layout<WBITS, BN>::kThreads), g.smem, a.stream, pdl,
                  g.ks, tx, tw, prm);
   if (st == QL_ERR_CUDA && g.ks > 1) {
     // a cluster launch the device refuses (resources taken by other work,
@@ -740,7 +740,7 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
     prm.stages = g.stages_unsplit;
     prm.nk_split = prm.nk;
     grid.z = 1;
-    st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::kThreads), g.smem_unsplit,
+    st = launch_ex(ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>, grid, dim3(ql::gemm::Layout<WBITS, BN>::kThreads), g.smem_unsplit,
                    a.stream, pdl, 1, tx, tw, prm);
   }
   return st;
@@ -942,8 +942,8 @@ int launch_dec_t(const LinearArgs& a, const DecPlan& d, const CUtensorMap& tw, c
     done[dev].store(1, std::memory_order_release);
   }
   dim3 grid((unsigned)d.tiles, 1, (unsigned)d.ks);
-  return launch_ex(kern, grid, dim3(ql::dec::kThreads), d.smem, a.stream, (a.flags & QL_FLAG_PDL) != 0, d.ks,
-                   tw, prm);
+  return launch_ex(kern, grid, dim3(ql::dec::kThreads), d.smem, a.stream,
+                   (a.flags & QL_FLAG_PDL) != 0, d.ks, tw, prm);
 }
 
 int run_dec(const LinearArgs& a, DeviceInfo* dev) {
