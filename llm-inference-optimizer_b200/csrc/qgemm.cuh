@@ -12,7 +12,10 @@
 //     stages is issued before waiting for the kernel before).  Per 128-k stage it loads the
 //     packed weight tile (128 rows x 64 B int4 / 128 B int8, 64/128-byte
 //     swizzle, a 3-D view of the rows) and the activation tile (BN rows x
-//     128 k as two 128-byte-swizzled K-major atoms).
+//     128 k as two 128-byte-swizzled K-major atoms), each completing on its
+//     own barrier: the decode of the first stages (up to the A slots in
+//     TMEM) runs while the kernel before finishes, and only the MMAs wait
+//     for the activations.
 //   * warps 2-9 (256 threads; thread = weight row = TMEM lane, two warps per
 //     lane quarter, each decoding one half of the stage's 128 k): read the
 //     row's packed bytes, decode them to fp16 in registers (int4: times the
@@ -22,15 +25,12 @@
 //   * warp 1 (one thread): issues tcgen05.mma.cta_group::1.kind::f16
 //     (A from TMEM, B from shared memory by descriptor, fp32 accumulator
 //     in TMEM) and tcgen05.commit's the stage back to producer/dequant.
-//     64-row activation tiles add a second issuer (warp 10) that takes the
-//     odd stages into a second accumulator: measured on B200, a thread
-//     issuing K = 16 MMAs back to back gets one through every ~57 cycles or
-//     more whatever N is, while two issuers together reach ~40 (N = 16) to
-//     ~64 (N = 128, the dense peak).  With it the 64-row tiles of the large
-//     layers run 6-11 % (int4) and up to 35 % (int8) faster; the 16- and
-//     32-row tiles, bound elsewhere, are unchanged or slower with it and
-//     keep one issuer.  The epilogue adds the two accumulators in a fixed
-//     order.
+//     Activation tiles of up to 64 rows add a second issuer (warp 10) that
+//     takes the odd stages into a second accumulator: measured on B200, a
+//     thread issuing K = 16 MMAs back to back gets one through every ~57
+//     cycles or more whatever N is, while two issuers together reach ~40
+//     (N = 16) to ~64 (N = 128, the dense peak).  The epilogue adds the two
+//     accumulators in a fixed order.
 //   * epilogue (warps 2-9, each half of the activation columns): tcgen05.ld
 //     of the accumulator(s), int8 row scale and bias in fp32, fp16 store (32
 //     consecutive n per warp per activation row).
@@ -56,10 +56,9 @@ namespace gemm {
 
 constexpr int kTileN = 128;     // weight rows per CTA = UMMA M
 constexpr int kBK = 128;        // k per stage = 8 MMAs of K=16
-// Warps: 0 producer, 1 MMA issuer, 2-9 dequant/epilogue, and (64-row
-// activation tiles) 10 the second MMA issuer; Layout::kThreads.
+// Warps: 0 producer, 1 MMA issuer, 2-9 dequant/epilogue, and (activation
+// tiles of up to 64 rows) 10 the second MMA issuer; Layout::kThreads.
 constexpr int kIssuer1Warp = 10;
-constexpr int kASlots = 2;      // A (dequantized weight) stages in TMEM
 
 struct Params {
   const void* scale;      // int8: [N] f32/f16; int4: [K/128, lds] f16
@@ -84,12 +83,20 @@ struct Layout {
   static constexpr int kXAtom = BN * 128;           // 64 k x BN rows of fp16
   static constexpr int kXStage = 2 * kXAtom;
   static constexpr int kStage = kXStage + kWStage;  // multiple of 1024
-  static constexpr uint32_t kTmemCols = BN + kASlots * 64 <= 256 ? 256 : 512;
-  static constexpr uint32_t kACol = BN <= 128 ? 128 : 256;  // first A column
+  // A (dequantized weight) stages in TMEM, 64 columns each from kACol: the
+  // narrow tiles' accumulator leaves room for three, so the decode runs
+  // three stages ahead of the MMAs (and, before the dependency wait, of
+  // the activations)
+  static constexpr int kASlots = BN <= 32 ? 3 : 2;
+  static constexpr uint32_t kACol = BN <= 32 ? 64 : BN <= 128 ? 128 : 256;  // first A column
+  static constexpr uint32_t kTmemCols = kACol + kASlots * 64 <= 256 ? 256 : 512;
   // second MMA issuer and accumulator (columns [BN, 2 BN), below kACol)
-  static constexpr bool kTwoIssuers = BN == 64;
+  static constexpr bool kTwoIssuers = BN <= 64;
   static constexpr int kThreads = kTwoIssuers ? 352 : 320;
-  static constexpr uint32_t kTx = kStage;
+  static_assert((kTwoIssuers ? 2 * BN : BN) <= (int)kACol, "accumulators overlap the A slots");
+  // mbarriers (wfull, xfull, wfree, xfree per stage, afull / afree per A
+  // slot, dfull), TMEM address and abort flag in the 256 bytes after the ring
+  static_assert((4 * 6 + 2 * kASlots + 1) * 8 + 8 <= 256, "barrier area");
   // Split-K reduction: narrow tiles push their partial into the members'
   // receive buffers (one cluster barrier); wide tiles park it in the
   // drained ring and the members pull (two barriers, no extra memory).
@@ -255,12 +262,17 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int S = p.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * L::kStage);
-  uint64_t* wfree = full + S;
+  // wfull: the stage's packed weights have landed (dequant waits); xfull:
+  // its activation tile has (the MMA waits).  Separate, so that the decode
+  // of the first stages does not wait for the activations, which only
+  // follow the dependency wait.
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + (size_t)S * L::kStage);
+  uint64_t* xfull = wfull + S;
+  uint64_t* wfree = xfull + S;
   uint64_t* xfree = wfree + S;
   uint64_t* afull = xfree + S;
-  uint64_t* afree = afull + kASlots;
-  uint64_t* dfull = afree + kASlots;
+  uint64_t* afree = afull + L::kASlots;
+  uint64_t* dfull = afree + L::kASlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);   // a wait of this CTA gave up
 
@@ -276,11 +288,12 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full + s, 1);
+      mbar_init(wfull + s, 1);
+      mbar_init(xfull + s, 1);
       mbar_init(wfree + s, 8);
       mbar_init(xfree + s, 1);
     }
-    for (int a = 0; a < kASlots; ++a) {
+    for (int a = 0; a < L::kASlots; ++a) {
       mbar_init(afull + a, 8);
       mbar_init(afree + a, 1);
     }
@@ -309,36 +322,49 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       const int pre = min(S, nk);
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = smem + (size_t)i * L::kStage;
-        mbar_arrive_expect_tx(full + i, L::kTx);
-        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, full + i, pol_w);
+        mbar_arrive_expect_tx(wfull + i, L::kWStage);
+        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, wfull + i, pol_w);
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = smem + (size_t)i * L::kStage;
-        tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, full + i, pol_x);
-        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, full + i, pol_x);
+        mbar_arrive_expect_tx(xfull + i, L::kXStage);
+        tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, xfull + i, pol_x);
+        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, xfull + i, pol_x);
       }
       int issued = pre;
+      bool xissued_last = true;     // the last issued stage's activations went out too
       for (int i = pre; i < nk; ++i) {
         const int s = i % S;
         const uint32_t par = ((i / S) - 1) & 1;
-        if (!mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait, abort) ||
-            !mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort)) {
+        uint8_t* st = smem + (size_t)s * L::kStage;
+        if (!mbar_wait(wfree + s, par, p.err, kDevErrEmptyWait, abort)) {
           *abort = 1;
           break;
         }
-        uint8_t* st = smem + (size_t)s * L::kStage;
-        mbar_arrive_expect_tx(full + s, L::kTx);
-        tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, full + s, pol_x);
-        tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, full + s, pol_x);
-        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, full + s, pol_w);
+        mbar_arrive_expect_tx(wfull + s, L::kWStage);
+        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, wfull + s, pol_w);
+        // stage i's weights are in flight; should its activation slot never
+        // free, the drain below waits for the weights alone
+        const bool xok = mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort);
+        if (xok) {
+          mbar_arrive_expect_tx(xfull + s, L::kXStage);
+          tma_load_2d(smem_u32(st), &tmap_x, (kbeg + i) * kBK, m0, xfull + s, pol_x);
+          tma_load_2d(smem_u32(st + L::kXAtom), &tmap_x, (kbeg + i) * kBK + 64, m0, xfull + s, pol_x);
+        }
         issued = i + 1;
+        if (!xok) {
+          *abort = 1;
+          xissued_last = false;
+          break;
+        }
       }
       // every issued copy lands before the CTA can exit (only the last
       // stage of each slot can still be in flight)
       for (int s = 0; s < min(issued, S); ++s) {
         const int last = s + ((issued - 1 - s) / S) * S;
-        mbar_wait(full + s, (last / S) & 1, p.err, kDevErrFullWait);
+        mbar_wait(wfull + s, (last / S) & 1, p.err, kDevErrFullWait);
+        if (xissued_last || last != issued - 1) mbar_wait(xfull + s, (last / S) & 1, p.err, kDevErrFullWait);
       }
     }
   } else if (warp == 1 || warp == kIssuer1Warp) {
@@ -348,9 +374,9 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       const uint32_t idesc = idesc_f16<BN>();
       const uint32_t d_tmem = tmem + (uint32_t)(q * BN);
       for (int i = q; i < nk; i += nissuers) {
-        const int s = i % S, a = i % kASlots;
-        if (!mbar_wait(full + s, (i / S) & 1, p.err, kDevErrMmaWait, abort) ||
-            !mbar_wait(afull + a, (i / kASlots) & 1, p.err, kDevErrMmaWait, abort)) {
+        const int s = i % S, a = i % L::kASlots;
+        if (!mbar_wait(xfull + s, (i / S) & 1, p.err, kDevErrMmaWait, abort) ||
+            !mbar_wait(afull + a, (i / L::kASlots) & 1, p.err, kDevErrMmaWait, abort)) {
           *abort = 1;
           break;
         }
@@ -385,12 +411,12 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
     };
     __half s_next = load_scale(0), s_next2 = load_scale(1);
     for (int i = 0; i < nk; ++i) {
-      const int s = i % S, a = i % kASlots;
+      const int s = i % S, a = i % L::kASlots;
       const __half s_cur = s_next;
       s_next = s_next2;
       s_next2 = load_scale(i + 2);
       // warp-uniform outcome: tcgen05.st below is warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(full + s, (i / S) & 1, p.err, kDevErrFullWait, abort))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(wfull + s, (i / S) & 1, p.err, kDevErrFullWait, abort))) {
         *abort = 1;
         break;
       }
@@ -456,8 +482,8 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(wfree + s);       // packed tile consumed
-      if (i >= kASlots &&
-          !__all_sync(0xffffffffu, mbar_wait(afree + a, ((i / kASlots) - 1) & 1, p.err, kDevErrFullWait, abort))) {
+      if (i >= L::kASlots &&
+          !__all_sync(0xffffffffu, mbar_wait(afree + a, ((i / L::kASlots) - 1) & 1, p.err, kDevErrFullWait, abort))) {
         *abort = 1;
         break;
       }
