@@ -318,13 +318,15 @@ int ql_linear_argmax_supported(int wbits, int64_t M, int64_t N, int64_t K);
  * N / groups columns; rank q owns columns [q*block, min(N/groups,
  * (q+1)*block)) of every block.  This rank's columns are either already in
  * `out` (src = NULL) or in src [M, groups*w] (lds; w = this rank's width per
- * block: gate columns, then up columns), then copied into out as well.  The
- * kernel stores them into every peer's gather buffer over NVLink — outputs
- * of up to 4 MiB as lines whose 8-byte words carry the call's epoch, larger
- * ones into banks followed by a flag per rank (system-scope release) — waits
- * (bounded) for every peer's columns and copies them into out: on
- * completion out holds all N columns on every rank.  All ranks make the same sequence of calls with the same
- * shapes.  Gather buffers: ql_gather_buffer_bytes(max_m, N) bytes, allocated
+ * block: gate columns, then up columns), then copied into out as well.
+ * Outputs of up to 4 MiB are pushed into every peer's gather buffer over
+ * NVLink as lines whose 8-byte words carry the call's epoch; larger ones are
+ * staged in this rank's own buffer, chunk by chunk, each chunk published by
+ * a ready flag (system-scope release), and every peer pulls them over
+ * NVLink once the flag has reached the call.  The kernel waits (bounded) for
+ * every peer's columns: on completion out holds all N columns on every
+ * rank.  All ranks make the same sequence of calls with the same shapes and
+ * equally aligned buffers.  Gather buffers: ql_gather_buffer_bytes(max_m, N) bytes, allocated
  * and shared with ql_xchg_alloc / ql_xchg_open / ql_xchg_close /
  * ql_xchg_free as the exchange buffers above (peers[rank] = own).  A wait
  * that runs out records QL_DEVICE_ERROR_PEER_WAIT. */

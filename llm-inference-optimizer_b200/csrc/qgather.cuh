@@ -7,11 +7,12 @@
 //
 // Every rank owns a gather buffer (plain device memory shared with the other
 // ranks of the node through CUDA IPC, zero-filled at allocation):
-//   [0, 32)     flags[kMaxRanks] u32: the last call whose columns rank q has
+//   [0, 8192)   ready[kMaxRanks][kMaxCtas] u32: ready[q][c] = the last call
+//               whose chunk c of rank q's columns CTA c of rank q has
 //               completely stored into this buffer (written by rank q)
-//   [32, 40)    state: counter u32 (CTAs arrived), epoch u32 (calls done);
+//   [8192, 8200) state: counter u32 (CTAs arrived), epoch u32 (calls done);
 //               only the owner touches them
-//   [256, ...)  data[2][max_m][ldb] fp16, ldb = N rounded up to 8: the other
+//   [8448, ...) data[2][max_m][ldb] fp16, ldb = N rounded up to 8: the other
 //               ranks' columns of a call, by epoch parity, at their global
 //               positions
 //   then        lines[2][line_rows][ldb / 4] 16-byte lines for small calls:
@@ -24,27 +25,36 @@
 // word (bounded) until both tags read e, so neither side needs a fence, a
 // counter or a flag — twice the bytes on NVLink, a few microseconds less
 // latency (used only when every rank owns columns: each rank then waits for
-// every peer's lines of a call).  Larger calls use the flagged protocol:
-//   1. every CTA stores its share of the rank's columns into data[e & 1] of
-//      every peer (16-byte stores when the shapes allow), makes them visible
-//      system-wide (fence.sc.sys) and counts itself in;
-//   2. the last CTA to arrive writes e into flags[rank] of every peer with a
-//      system-scope release;
-//   3. every CTA takes the peers in turn: one thread polls (bounded, acquire)
-//      until the peer's flag has reached e, then the CTA copies its share of that
-//      peer's columns from data[e & 1] into `out`.
-// A rank waits for every peer's flag of a call before it finishes the call,
-// so it is at most one call ahead of any peer: when it stores call e + 2
-// into a peer's bank e & 1, that peer has finished call e + 1, and with it
-// its copy out of call e's bank.  Two banks are therefore enough.  The same
-// bound means a waiting rank may find a peer's flag already at e + 1 (the
-// peer finished call e and stored call e + 1 into the other bank), so the
-// wait is for the flag to have reached e (wrap-safe: (int)(flag - e) >= 0),
-// not for it to equal e.  The grid
-// is at most one CTA per SM, so all CTAs of a rank are resident together and
-// no CTA waits on one that cannot run.  Ranks must make the same sequence of
-// calls.  A wait that runs out sets kDevErrPeerWait in the device error word
-// and the kernel carries on (the affected columns are then stale).
+// every peer's lines of a call).  Larger calls go through the banks, chunk
+// by chunk: the G CTAs of a launch (the same G on every rank: it depends
+// only on the shapes) split each rank's columns into G contiguous chunks of
+// units, and CTA c of every rank handles chunk c of every rank's columns:
+//   1. CTA c stores chunk c of this rank's columns into data[e & 1] of every
+//      peer (16-byte stores when the shapes allow), makes them visible
+//      system-wide (fence.sc.sys) and writes ready[rank][c] = e into every
+//      peer's buffer with a system-scope release;
+//   2. it takes the peers in turn: one thread polls its own ready[q][c]
+//      (bounded, acquire) until it has reached e, then the CTA copies chunk
+//      c of q's columns from its own data[e & 1] into `out`.
+// No CTA waits for the other CTAs of its rank, so the copies out of the
+// bank start chunk by chunk as the peers' chunks land.  (Measured on two
+// B200s, M = 16 / 64 of a 151936-wide output: one flag per rank, set by the
+// last CTA to finish, went out ~4.5 us after the median CTA's fence; pulling
+// the chunks over NVLink instead of pushing them was 7-12 % slower.)
+// Every CTA waits for every peer's ready[q][c] in every call, whether or
+// not chunk c holds columns.  A rank finishes call e + 1 only once CTA c of
+// every peer has published ready[q][c] = e + 1, which that CTA does in its
+// call e + 1, after the peer's call e — and with it the peer's copies out
+// of bank e & 1 — has completed; so when this rank stores call e + 2 into a
+// peer's bank e & 1, that peer no longer reads call e there.  Two banks are
+// therefore enough.  The same bound means a peer's ready[q][c] may already
+// be at e + 1 (it has moved on to the other bank), so the wait is for it to
+// have reached e (wrap-safe: (int)(flag - e) >= 0), not to equal it.  The grid
+// is at most one CTA per SM, so all CTAs of a rank are resident together.
+// Ranks must make the same sequence of calls with the same shapes and
+// equally aligned buffers (the alignment picks the protocol).  A wait that runs out sets
+// kDevErrPeerWait in the device error word and the kernel carries on (the
+// affected columns are then stale).
 #pragma once
 
 #include "ql_common.cuh"
@@ -53,6 +63,7 @@ namespace ql {
 namespace gather {
 
 constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 256;   // CTAs of one gather launch (ready flags per rank)
 constexpr long long kLineMaxPayload = 4ll << 20;   // bytes of output [M, N] fp16 sent as tagged lines
 constexpr int kBatch = 4;    // loads a thread keeps in flight before its stores (push and copy loops)
 
@@ -64,8 +75,8 @@ struct Layout {
 __host__ __device__ inline Layout layout(int max_m, long long n) {
   Layout l;
   l.flags = 0;
-  l.state = kMaxRanks * 4;
-  l.data = 256;
+  l.state = (size_t)kMaxRanks * kMaxCtas * 4;
+  l.data = l.state + 256;
   l.ldb = (n + 7) / 8 * 8;
   l.lines = (l.data + (size_t)2 * max_m * l.ldb * 2 + 255) / 256 * 256;
   const long long fit = kLineMaxPayload / (2 * l.ldb);
@@ -81,7 +92,9 @@ struct Params {
   long long ldo;
   long long ng, block;    // columns per group; shard width per group
   int M, groups, rank, world, max_m;
-  int vec;                // 16-byte path: 8-aligned offsets, widths and strides
+  int cw;                 // columns per unit of the flagged protocol: 8 when ng and block are
+                          // multiples of 8, else 1 (shapes only: the same on every rank)
+  int vec;                // 16-byte accesses (cw == 8, 16-byte aligned pointers and strides)
   int lines;              // tagged-line protocol (4-aligned offsets, widths, strides; M <= line_rows)
   unsigned char* peer[kMaxRanks];   // gather buffer of every rank (peer[rank] = own)
   unsigned* err;
@@ -221,7 +234,6 @@ __device__ __forceinline__ void gather_lines(const Params& p, const Layout& L, u
 
 __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
   __shared__ unsigned done_s;
-  __shared__ int last_s;
   griddep_wait();   // this rank's columns come from the kernel before
 
   const Layout L = layout(p.max_m, (long long)p.groups * p.ng);
@@ -237,28 +249,35 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
     return;
   }
   const size_t bank = (size_t)(e & 1u) * p.max_m * L.ldb;
-  const long long nthr = (long long)gridDim.x * blockDim.x;
-  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int vw = p.vec ? 8 : 1;   // elements per unit (ng and block are multiples of it)
-  const long long ngu = p.ng / vw, bu = p.block / vw;
-
-  // ---- 1. push this rank's columns to every peer (and into out if staged)
-  {
-    const long long wu = shard_width(p, p.rank) / vw;
+  const long long ngu = p.ng / p.cw, bu = p.block / p.cw;
+  // chunk c of rank q's columns: units [c * U / G, (c + 1) * U / G) of its
+  // [M, groups*w] slice, U = M * groups * w / cw.  cw, G and the shard
+  // widths depend on the shapes alone, so every rank splits rank q's
+  // columns the same way.
+  auto chunk = [&](int q, long long& wu, long long& u0, long long& u1) {
+    wu = shard_width(p, q) / p.cw;
     const long long units = (long long)p.M * p.groups * wu;
+    u0 = units * blockIdx.x / gridDim.x;
+    u1 = units * (blockIdx.x + 1) / gridDim.x;
+  };
+
+  // ---- 1. this rank's chunk into every peer's bank (and into out if staged)
+  {
+    long long wu, u0, u1;
+    chunk(p.rank, wu, u0, u1);
     if (p.vec) {
-      for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+      for (long long i0 = u0 + threadIdx.x; i0 < u1; i0 += kBatch * blockDim.x) {
         uint4 v[kBatch];
         int mm[kBatch];
         long long cc[kBatch];
         #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-          const long long i = i0 + u * nthr;
+          const long long i = i0 + u * blockDim.x;
           mm[u] = -1;
-          if (i < units) {
+          if (i < u1) {
             long long j;
             locate(p.groups, ngu, bu, p.rank, wu, i, mm[u], j, cc[u]);
-            cc[u] *= vw;
+            cc[u] *= 8;
             v[u] = p.src ? *reinterpret_cast<const uint4*>(p.src + (long long)mm[u] * p.lds + j * 8)
                          : __ldcg(reinterpret_cast<const uint4*>(p.out + (long long)mm[u] * p.ldo + cc[u]));
           }
@@ -275,43 +294,43 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
         }
       }
     } else {
-      for (long long i = tid; i < units; i += nthr) {
+      for (long long i = u0 + threadIdx.x; i < u1; i += blockDim.x) {
         int m;
         long long j, col;
         locate(p.groups, ngu, bu, p.rank, wu, i, m, j, col);
-        const __half v = p.src ? p.src[(long long)m * p.lds + j] : p.out[(long long)m * p.ldo + col];
-        if (p.src) p.out[(long long)m * p.ldo + col] = v;
-        for (int k = 1; k < p.world; ++k) {
-          const int q = (p.rank + k) % p.world;
-          reinterpret_cast<__half*>(p.peer[q] + L.data)[bank + (long long)m * L.ldb + col] = v;
+        for (int t = 0; t < p.cw; ++t) {
+          const long long jj = j * p.cw + t, cl = col * p.cw + t;
+          const __half v = p.src ? p.src[(long long)m * p.lds + jj] : p.out[(long long)m * p.ldo + cl];
+          if (p.src) p.out[(long long)m * p.ldo + cl] = v;
+          for (int k = 1; k < p.world; ++k) {
+            const int q = (p.rank + k) % p.world;
+            reinterpret_cast<__half*>(p.peer[q] + L.data)[bank + (long long)m * L.ldb + cl] = v;
+          }
         }
       }
     }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();   // this CTA's peer stores, before it counts itself in
-    last_s = atomic_add_acq_rel_gpu(counter, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-
-  // ---- 2. the last CTA: every CTA's stores are out, tell the peers
-  if (last_s && threadIdx.x == 0) {
-    *reinterpret_cast<volatile unsigned*>(counter) = 0u;        // all CTAs have arrived
-    *reinterpret_cast<volatile unsigned*>(epoch_done) = e;      // all CTAs have read it
-    __threadfence_system();
+    __threadfence_system();   // the CTA's peer stores, before it publishes them
     for (int k = 1; k < p.world; ++k) {
       const int q = (p.rank + k) % p.world;
-      st_release_sys(reinterpret_cast<unsigned*>(p.peer[q] + L.flags) + p.rank, e);
+      st_release_sys(reinterpret_cast<unsigned*>(p.peer[q] + L.flags) + p.rank * kMaxCtas + blockIdx.x, e);
+    }
+    // the epoch advances once every CTA has read it (local bookkeeping only)
+    if (atomicAdd(counter, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned*>(counter) = 0u;
+      *reinterpret_cast<volatile unsigned*>(epoch_done) = e;
     }
   }
 
-  // ---- 3. peers in turn: wait for the flag, copy the columns out
-  const __half* data = reinterpret_cast<const __half*>(own + L.data) + bank;
+  // ---- 2. peers in turn: wait for their chunk c, copy it out of the bank
   for (int k = 1; k < p.world; ++k) {
     const int q = (p.rank + k) % p.world;
+    long long wu, u0, u1;
+    chunk(q, wu, u0, u1);
     if (threadIdx.x == 0) {
-      const unsigned* f = flags + q;
+      const unsigned* f = flags + q * kMaxCtas + blockIdx.x;
       if (!flag_reached(ld_acquire_sys(f), e)) {
         const long long t0 = clock64();
         while (!flag_reached(ld_acquire_sys(f), e)) {
@@ -324,21 +343,20 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
       }
     }
     __syncthreads();
-    const long long wu = shard_width(p, q) / vw;
-    const long long units = (long long)p.M * p.groups * wu;
+    const __half* data = reinterpret_cast<const __half*>(own + L.data) + bank;
     if (p.vec) {
-      for (long long i0 = tid; i0 < units; i0 += kBatch * nthr) {
+      for (long long i0 = u0 + threadIdx.x; i0 < u1; i0 += kBatch * blockDim.x) {
         uint4 v[kBatch];
         int mm[kBatch];
         long long cc[kBatch];
         #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-          const long long i = i0 + u * nthr;
+          const long long i = i0 + u * blockDim.x;
           mm[u] = -1;
-          if (i < units) {
+          if (i < u1) {
             long long j;
             locate(p.groups, ngu, bu, q, wu, i, mm[u], j, cc[u]);
-            cc[u] *= vw;
+            cc[u] *= 8;
             v[u] = __ldcg(reinterpret_cast<const uint4*>(data + (long long)mm[u] * L.ldb + cc[u]));
           }
         }
@@ -347,12 +365,14 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
           if (mm[u] >= 0) *reinterpret_cast<uint4*>(p.out + (long long)mm[u] * p.ldo + cc[u]) = v[u];
       }
     } else {
-      for (long long i = tid; i < units; i += nthr) {
+      for (long long i = u0 + threadIdx.x; i < u1; i += blockDim.x) {
         int m;
         long long j, col;
         locate(p.groups, ngu, bu, q, wu, i, m, j, col);
-        col *= vw;
-        p.out[(long long)m * p.ldo + col] = __ldcg(data + (long long)m * L.ldb + col);
+        for (int t = 0; t < p.cw; ++t) {
+          const long long cl = col * p.cw + t;
+          p.out[(long long)m * p.ldo + cl] = __ldcg(data + (long long)m * L.ldb + cl);
+        }
       }
     }
   }

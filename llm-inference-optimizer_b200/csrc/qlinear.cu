@@ -1557,8 +1557,8 @@ int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64
   p.rank = rank;
   p.world = world;
   p.max_m = max_m;
-  p.vec = aligned16(out) && ldo % 8 == 0 && ng % 8 == 0 && block % 8 == 0 &&
-          (!src || (aligned16(src) && lds % 8 == 0));
+  p.cw = ng % 8 == 0 && block % 8 == 0 ? 8 : 1;
+  p.vec = p.cw == 8 && aligned16(out) && ldo % 8 == 0 && (!src || (aligned16(src) && lds % 8 == 0));
   // small calls as tagged lines (8-byte column runs: 4-aligned offsets,
   // widths and strides), the rest through the flagged banks.  Lines only
   // when every rank owns columns: a reader waits for the lines of each peer
@@ -1572,9 +1572,12 @@ int ql_allgather_f16(const void* src, int64_t lds, void* out, int64_t ldo, int64
   for (int q = 0; q < world; ++q) p.peer[q] = static_cast<unsigned char*>(peers[q]);
   p.err = dev->err_word;
   // one CTA per SM at most (every CTA waits on the peers: all must be
-  // resident together), fewer when there is little to move
-  const int64_t units = M * N / (p.lines ? 4 : p.vec ? 8 : 1);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(dev->sms, cdiv(units, 512 * 4)));
+  // resident together), fewer when there is little to move.  The flagged
+  // protocol's grid depends on the shapes alone: CTA c of every rank
+  // handles chunk c of every rank's columns.
+  const int64_t units = M * N / (p.lines ? 4 : p.cw);
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>(std::min(dev->sms, ql::gather::kMaxCtas), cdiv(units, 512 * 4)));
   return launch(ql::gather::allgather_kernel, dim3((unsigned)grid), dim3(512), 0, static_cast<cudaStream_t>(stream),
                 (flags & QL_FLAG_PDL) != 0, p);
 }

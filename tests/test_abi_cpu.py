@@ -115,7 +115,7 @@ def test_gather_argument_checks_without_gpu():
     lib = _lib.load()
     assert lib.ql_gather_buffer_bytes(0, 1024) == 0
     assert lib.ql_gather_buffer_bytes(4, 0) == 0
-    assert lib.ql_gather_buffer_bytes(4, 1001) >= 256 + 2 * 4 * 1008 * 2
+    assert lib.ql_gather_buffer_bytes(4, 1001) >= 8448 + 2 * 4 * 1008 * 2
     assert lib.ql_gather_buffer_bytes(4, 1001) % 256 == 0
     names = ["src", "lds", "out", "ldo", "M", "N", "groups", "block", "rank", "world", "max_m", "peers",
              "flags", "stream"]
