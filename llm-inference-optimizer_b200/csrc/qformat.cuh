@@ -248,9 +248,36 @@ __global__ void __launch_bounds__(128) quantize_int4_kernel(const __half* w, lon
 // the caller's workspace, which must be left zero-filled (split-K scratch
 // shares it), so every element is cleared after it is read.
 __global__ void __launch_bounds__(256) swiglu_kernel(__half* y, long long ldy, int M, int nh, __half* out,
-                                                     long long ldo) {
-  const long long total = (long long)M * nh;
+                                                     long long ldo, int vec) {
+  griddep_wait();   // y comes from the kernel before
+  griddep_launch_dependents();
   const __half zero = __float2half(0.f);
+  if (vec) {
+    // 8 columns per thread: 16-byte loads of gate and up, 16-byte stores
+    const int nv = nh / 8;
+    const long long total = (long long)M * nv;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int m = (int)(i / nv), n = (int)(i - (long long)m * nv) * 8;
+      uint4* gp = reinterpret_cast<uint4*>(y + (long long)m * ldy + n);
+      uint4* up = reinterpret_cast<uint4*>(y + (long long)m * ldy + nh + n);
+      const uint4 gv = *gp, uv = *up;
+      *gp = make_uint4(0u, 0u, 0u, 0u);
+      *up = make_uint4(0u, 0u, 0u, 0u);
+      const __half* gh = reinterpret_cast<const __half*>(&gv);
+      const __half* uh = reinterpret_cast<const __half*>(&uv);
+      uint4 ov;
+      __half* oh = reinterpret_cast<__half*>(&ov);
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float g = __half2float(gh[j]);
+        oh[j] = __float2half_rn(g / (1.f + __expf(-g)) * __half2float(uh[j]));
+      }
+      *reinterpret_cast<uint4*>(out + (long long)m * ldo + n) = ov;
+    }
+    return;
+  }
+  const long long total = (long long)M * nh;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int m = (int)(i / nh), n = (int)(i - (long long)m * nh);

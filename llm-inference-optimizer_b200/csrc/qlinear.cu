@@ -1105,11 +1105,14 @@ int run_swiglu(const LinearArgs& a) {
   b.ws_bytes = a.ws_bytes - temp;
   st = run_linear(b);
   if (st != QL_OK) return st;
-  const long long total = a.M * n;
-  const unsigned blocks = (unsigned)std::min<int64_t>(cdiv(total, 256), 65535LL * 8);
-  return launch(ql::fmt::swiglu_kernel, dim3(blocks), dim3(256), 0, a.stream, false,
+  // 8 columns per thread where n, ldo and out allow 16-byte accesses (the
+  // temporary is 256-byte aligned with a row stride of 2n)
+  const int vec = n % 8 == 0 && a.ldo % 8 == 0 && aligned16(a.out) && aligned16(a.ws);
+  const long long total = a.M * n / (vec ? 8 : 1);
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), 65535LL * 8));
+  return launch(ql::fmt::swiglu_kernel, dim3(blocks), dim3(256), 0, a.stream, (a.flags & QL_FLAG_PDL) != 0,
                 static_cast<__half*>(a.ws), (long long)(2 * n), (int)a.M, (int)n,
-                static_cast<__half*>(a.out), (long long)a.ldo);
+                static_cast<__half*>(a.out), (long long)a.ldo, vec);
 }
 
 // Exchange context of one call; QL_OK or the status for bad arguments.
