@@ -70,8 +70,25 @@ struct Params {
   int nk_split;           // stages per K-split (gridDim.z splits = cluster size)
   int stages;             // shared-memory ring depth
   int scale_f32, bias_f32;
+  // SwiGLU mode (nh > 0): the weight is a stacked [gate; up] of 2*nh rows
+  // and out[M, nh] = silu(x gate^T) * (x up^T).  Tile x then holds gate
+  // rows [64x, 64x + 64) in its TMEM lanes 0-63 and the matching up rows
+  // in lanes 64-127 (two 64-row weight boxes per stage), so both factors of
+  // an output meet in one CTA.  Unsplit launches and pull-mode K-splits.
+  int nh;
   unsigned* err;
 };
+
+// Weight row held in TMEM lane r of tile `tile` (-1: past the weight).
+__device__ __forceinline__ int tile_row(const Params& p, int tile, int r) {
+  if (p.nh == 0) {
+    const int n = tile * kTileN + r;
+    return n < p.N ? n : -1;
+  }
+  const int c = tile * (kTileN / 2) + (r & (kTileN / 2 - 1));   // output column
+  if (c >= p.nh) return -1;
+  return r < kTileN / 2 ? c : p.nh + c;
+}
 
 // Largest K-split = thread-block cluster size (beyond the portable 8: the
 // kernels are marked for non-portable cluster sizes, which B200 runs up to 16).
@@ -254,6 +271,63 @@ __device__ __forceinline__ void reduce_slice(const Params& p, uint32_t base, int
   }
 }
 
+// SwiGLU mode of the pull reduction: pairs [q0, q1) of the tile, pair
+// q = m*64 + c joining gate element m*128 + c and up element m*128 + 64 + c;
+// each is summed over the ks members in rank order, finished with its own
+// scale and bias, and silu(gate) * up is stored once (fp32, one rounding).
+template <int WBITS, int EB, int KS>
+__device__ __forceinline__ void reduce_pairs(const Params& p, uint32_t base, int ks, int q0, int q1, int tid,
+                                             int tile, int m0) {
+  constexpr int kStride = 256;
+  constexpr int kHalfRows = kTileN / 2;
+  #pragma unroll 1
+  for (int qb = q0 + tid; qb < q1; qb += EB * kStride) {
+    float tg[EB][KS], tu[EB][KS];
+    #pragma unroll
+    for (int q = 0; q < KS; ++q) {
+      const uint32_t peer = q < ks ? dsmem_addr(base, (uint32_t)q) : 0u;
+      #pragma unroll
+      for (int u = 0; u < EB; ++u) {
+        const int pq = qb + u * kStride;
+        const int e = (pq / kHalfRows) * kTileN + (pq % kHalfRows);
+        const bool ok = q < ks && pq < q1;
+        tg[u][q] = ok ? ld_dsmem_f32(peer + (uint32_t)e * 4u) : 0.f;
+        tu[u][q] = ok ? ld_dsmem_f32(peer + (uint32_t)(e + kHalfRows) * 4u) : 0.f;
+      }
+    }
+    #pragma unroll
+    for (int u = 0; u < EB; ++u) {
+      const int pq = qb + u * kStride;
+      float gv = 0.f, uv = 0.f;
+      #pragma unroll
+      for (int q = 0; q < KS; ++q) {                 // rank order; padding adds +0
+        gv += tg[u][q];
+        uv += tu[u][q];
+      }
+      const int c = tile * kHalfRows + (pq % kHalfRows);
+      const int m = m0 + pq / kHalfRows;
+      if (pq < q1 && c < p.nh && m < p.M) {
+        float sg = 1.f, su = 1.f, bg = 0.f, bu = 0.f;
+        if (WBITS == 8) {
+          sg = p.scale_f32 ? static_cast<const float*>(p.scale)[c]
+                           : __half2float(static_cast<const __half*>(p.scale)[c]);
+          su = p.scale_f32 ? static_cast<const float*>(p.scale)[p.nh + c]
+                           : __half2float(static_cast<const __half*>(p.scale)[p.nh + c]);
+        }
+        if (p.bias) {
+          bg = p.bias_f32 ? static_cast<const float*>(p.bias)[c]
+                          : __half2float(static_cast<const __half*>(p.bias)[c]);
+          bu = p.bias_f32 ? static_cast<const float*>(p.bias)[p.nh + c]
+                          : __half2float(static_cast<const __half*>(p.bias)[p.nh + c]);
+        }
+        gv = fmaf(gv, sg, bg);
+        uv = fmaf(uv, su, bu);
+        p.out[(long long)m * p.ldo + c] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
+      }
+    }
+  }
+}
+
 template <int WBITS, int LAYOUT, int BN>
 __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -316,6 +390,17 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       prefetch_tmap(&tmap_w);
       const uint64_t pol_w = l2_policy_evict_last();   // reused by every activation tile
       const uint64_t pol_x = l2_policy_evict_last();   // reused by every weight tile
+      // one 128-row box, or (SwiGLU mode) the gate and up halves as two
+      // 64-row boxes (the map's box is then 64 rows high)
+      auto load_w = [&](uint8_t* st, int kstage, uint64_t* bar) {
+        if (p.nh == 0) {
+          tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kstage, n0, bar, pol_w);
+        } else {
+          const int c0 = blockIdx.x * (kTileN / 2);
+          tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kstage, c0, bar, pol_w);
+          tma_load_3d(smem_u32(st + L::kXStage + L::kWStage / 2), &tmap_w, 0, kstage, p.nh + c0, bar, pol_w);
+        }
+      };
       // The weights of the first ring-full of stages do not depend on the
       // kernel before (programmatic dependent launch): they stream while it
       // finishes; the activations follow once it has.
@@ -323,7 +408,7 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = smem + (size_t)i * L::kStage;
         mbar_arrive_expect_tx(wfull + i, L::kWStage);
-        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, wfull + i, pol_w);
+        load_w(st, kbeg + i, wfull + i);
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i) {
@@ -343,7 +428,7 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(wfull + s, L::kWStage);
-        tma_load_3d(smem_u32(st + L::kXStage), &tmap_w, 0, kbeg + i, n0, wfull + s, pol_w);
+        load_w(st, kbeg + i, wfull + s);
         // stage i's weights are in flight; should its activation slot never
         // free, the drain below waits for the weights alone
         const bool xok = mbar_wait(xfree + s, par, p.err, kDevErrEmptyWait, abort);
@@ -402,12 +487,12 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
     const int quarter = warp & 3;                 // TMEM lane quarter of this warp
     const int half = (warp - 2) >> 2;             // which 64 k of the stage (and half of the columns)
     const int r = quarter * 32 + lane;            // weight row within the tile = TMEM lane
-    const int n = n0 + r;
+    const int n = tile_row(p, blockIdx.x, r);     // its row in the weight, -1 past it
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const __half* sc4 = static_cast<const __half*>(p.scale);
     // int4 group scale of this row for stage i (0 past N), two stages ahead
     auto load_scale = [&](int i) -> __half {
-      return (WBITS == 4 && i < nk && n < p.N) ? sc4[(long long)(kbeg + i) * p.lds + n] : __float2half(0.f);
+      return (WBITS == 4 && i < nk && n >= 0) ? sc4[(long long)(kbeg + i) * p.lds + n] : __float2half(0.f);
     };
     __half s_next = load_scale(0), s_next2 = load_scale(1);
     for (int i = 0; i < nk; ++i) {
@@ -519,7 +604,7 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       }
     };
     float sc8 = 1.f, bv = 0.f;
-    if (n < p.N) {
+    if (n >= 0) {
       if (WBITS == 8)
         sc8 = p.scale_f32 ? static_cast<const float*>(p.scale)[n]
                           : __half2float(static_cast<const __half*>(p.scale)[n]);
@@ -528,12 +613,39 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
                         : __half2float(static_cast<const __half*>(p.bias)[n]);
     }
     constexpr int kHalfCols = BN / 2;
-    if (gridDim.z == 1) {
+    if (gridDim.z == 1 && p.nh > 0) {
+      // SwiGLU, unsplit: every epilogue warp parks its finished fp32 values
+      // in the drained ring as [gate | up][column m][row c] (lanes 0-63 hold
+      // gate rows, 64-127 the matching up rows), the warps meet, and all
+      // 256 threads combine the pairs: silu and product in fp32, one
+      // rounding to fp16, 64 consecutive output columns per activation row
+      float* buf = reinterpret_cast<float*>(smem);
+      constexpr int kHalfRows = kTileN / 2;
+      const int sel = r >= kHalfRows ? 1 : 0, hr = r & (kHalfRows - 1);
       #pragma unroll 1
       for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
         uint32_t v[8];
         ld_acc(tmem + lane_base + (uint32_t)c0, v);
-        if (n < p.N) {
+        #pragma unroll
+        for (int j = 0; j < 8; ++j)
+          buf[(sel * BN + c0 + j) * kHalfRows + hr] = fmaf(__uint_as_float(v[j]), sc8, bv);
+      }
+      named_bar_sync(1, 256);
+      #pragma unroll 4
+      for (int idx = (int)threadIdx.x - 64; idx < BN * kHalfRows; idx += 256) {
+        const int ml = idx / kHalfRows, c = idx % kHalfRows;
+        const int col = blockIdx.x * kHalfRows + c, m = m0 + ml;
+        if (col < p.nh && m < p.M) {
+          const float gv = buf[idx], uv = buf[BN * kHalfRows + idx];
+          p.out[(long long)m * p.ldo + col] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
+        }
+      }
+    } else if (gridDim.z == 1) {
+      #pragma unroll 1
+      for (int c0 = half * kHalfCols; c0 < (half + 1) * kHalfCols; c0 += 8) {
+        uint32_t v[8];
+        ld_acc(tmem + lane_base + (uint32_t)c0, v);
+        if (n >= 0) {
           #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int m = m0 + c0 + j;
@@ -621,10 +733,18 @@ __global__ void __launch_bounds__(Layout<WBITS, BN>::kThreads, 1)
       // summed (one remote round trip per batch): 8 elements x up to 4
       // members, or 2 elements x up to 16 (32 registers, so that the narrow
       // tiles still run two CTAs per SM)
-      if (ks <= 4)
+      if (p.nh > 0) {
+        constexpr int P = BN * kTileN / 2;          // gate/up pairs of the tile
+        const int q0 = (int)(me * P / ks), q1 = (int)((me + 1) * P / ks);
+        if (ks <= 4)
+          reduce_pairs<WBITS, 4, 4>(p, smem_u32(smem), ks, q0, q1, (int)threadIdx.x - 64, blockIdx.x, m0);
+        else
+          reduce_pairs<WBITS, 1, kMaxSplits>(p, smem_u32(smem), ks, q0, q1, (int)threadIdx.x - 64, blockIdx.x, m0);
+      } else if (ks <= 4) {
         reduce_slice<WBITS, 8, 4>(p, smem_u32(smem), ks, e0, e1, (int)threadIdx.x - 64, n0, m0);
-      else
+      } else {
         reduce_slice<WBITS, 2, kMaxSplits>(p, smem_u32(smem), ks, e0, e1, (int)threadIdx.x - 64, n0, m0);
+      }
     }
     cluster_sync_all();                 // no member leaves while its partial may still be read
   }

@@ -154,12 +154,12 @@ int make_act_map(CUtensorMap* tm, const void* base, uint64_t K, uint64_t rows, u
 // Packed weight rows as [N][kbytes/C][C] with one C-byte stage per row per
 // box (C = 64 for int4, 128 for int8) and the matching swizzle.
 int make_gemm_weight_map(CUtensorMap* tm, const void* base, uint64_t kbytes, uint64_t rows, uint64_t row_stride,
-                         int chunk) {
+                         int chunk, int box_rows = 128) {
   auto fn = encode_fn();
   if (!fn) return QL_ERR_DEVICE;
   cuuint64_t dims[3] = {(cuuint64_t)chunk, kbytes / chunk, rows};
   cuuint64_t strides[2] = {(cuuint64_t)chunk, row_stride};
-  cuuint32_t box[3] = {(cuuint32_t)chunk, 1, 128};
+  cuuint32_t box[3] = {(cuuint32_t)chunk, 1, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, chunk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
@@ -727,8 +727,16 @@ int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap&
   GemmLaunch g;
   int st = gemm_launch_plan<WBITS, LAYOUT, BN>(tiles, prm.nk, &g);
   if (st != QL_OK) return st;
+  if (prm.nh > 0 && ql::gemm::Layout<WBITS, BN>::kPush && g.ks > 1) {
+    // SwiGLU mode has no push-mode reduction: the narrow tiles run unsplit
+    g.ks = 1;
+    g.nk_split = prm.nk;
+    g.stages = g.stages_unsplit;
+    g.smem = g.smem_unsplit;
+  }
   prm.stages = g.stages;
   prm.nk_split = g.nk_split;
+  // (SwiGLU mode: 64 output columns per tile, cdiv(N / 2, 64) = cdiv(N, 128) tiles)
   dim3 grid((unsigned)cdiv(a.N, ql::gemm::kTileN), (unsigned)cdiv(a.M, BN), (unsigned)g.ks);
   if (grid.y > 65535 || grid.z > 65535) return QL_ERR_BAD_SHAPE;
   const bool pdl = (a.flags & QL_FLAG_PDL) != 0;
@@ -794,7 +802,9 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
   CUtensorMap tx, tw;
   int st = make_act_map(&tx, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx, bn);
   if (st != QL_OK) return st;
-  st = make_gemm_weight_map(&tw, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, WBITS == 4 ? 64 : 128);
+  // SwiGLU mode loads the gate and up halves of a tile as two 64-row boxes
+  st = make_gemm_weight_map(&tw, a.w, kbytes, (uint64_t)a.N, (uint64_t)a.ldw, WBITS == 4 ? 64 : 128,
+                            a.swiglu_n > 0 ? ql::gemm::kTileN / 2 : ql::gemm::kTileN);
   if (st != QL_OK) return st;
   ql::gemm::Params p;
   p.scale = a.scale;
@@ -810,6 +820,7 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
   p.stages = 0;
   p.scale_f32 = a.scale_dtype == QL_DTYPE_F32;
   p.bias_f32 = a.bias_dtype == QL_DTYPE_F32;
+  p.nh = (int)a.swiglu_n;
   p.err = dev->err_word;
   switch (bn) {
     case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.tiles);
@@ -978,15 +989,22 @@ int run_dec(const LinearArgs& a, DeviceInfo* dev) {
 }
 
 // Where the tensor-core GEMM replaces the decode kernel (measured on B200:
-// forced-path sweeps of both over M = 8..32 on the config-1 to 4 shapes):
-// from 24 batch rows always (the decode kernel re-decodes the weights for
-// every 16-row batch chunk); below that only where the decode kernel would
-// need a K-split through the workspace — tall-K layers (K >= 3N) from 12
-// rows (from 8 when K >= 12288), and layers with K >= 4096 wider than 12288
-// (up/gate of 7B-class models, their lm_heads) from 12.  Small (q/k/v/o)
-// and shallow wide layers stay on the decode kernel up to 23 rows.
+// forced-path sweeps of both over M = 8..64 on the config-1 to 4 shapes):
+// from 24 batch rows (the decode kernel re-decodes the weights for every
+// 16-row batch chunk); below that where the decode kernel would need a
+// K-split through the workspace — tall-K layers (K >= 3N) from 12 rows
+// (from 8 when K >= 12288), and layers with K >= 4096 wider than 12288
+// (up/gate of 7B-class models, their lm_heads) from 12.  Small layers (at
+// most 4 Mi weights: q/k/v/o of 1.5B-class models) differ: their weights
+// stay in L2 across the batch chunks, so the decode kernel keeps them up
+// to 64 rows from 24 (int8) / 48 (int4) rows — 1536x1536 / 1536x2048 at
+// M 64: int8 6.3 / 6.3 us against 6.9 / 7.3, int4 6.4 / 6.3 against 6.6 /
+// 7.0 — and int4 takes the GEMM from 16 rows (4.1 / 4.3 us against 4.3 /
+// 4.4 at M 16).
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
-  (void)wbits;
+  const bool small = N * K <= (int64_t)1 << 22;
+  if (small && M <= 64 && M >= (wbits == 8 ? 24 : 48)) return false;
+  if (small && wbits == 4 && M >= 16 && N >= 1024) return true;
   if (M >= 24) return true;
   if (M < 8) return false;
   if (K >= 3 * N && (M >= 12 || K >= 12288)) return true;
@@ -1070,9 +1088,11 @@ int run_linear(const LinearArgs& a) {
 
 // Fused gate+up with SwiGLU: weights are 2n stacked rows (gate, then up),
 // out[M, n] = silu(x @ gate^T) * (x @ up^T).  The decode kernel does it in
-// its epilogue when the dispatch picks it and it has a K-unsplit plan;
-// otherwise the [M, 2n] product goes through the workspace and an
-// elementwise kernel applies SwiGLU.
+// its epilogue when the dispatch picks it and it has a K-unsplit plan, the
+// tensor-core kernel in its epilogue when the dispatch picks that (tiles of
+// 64 gate rows and the matching 64 up rows); otherwise (unaligned operands,
+// forced portable kernel, no unsplit decode plan) the [M, 2n] product goes
+// through the workspace and an elementwise kernel applies SwiGLU.
 size_t swiglu_temp_bytes(int64_t M, int64_t n) { return ((size_t)M * 2 * n * 2 + 255) / 256 * 256; }
 
 bool swiglu_fused_plan(int wbits, int64_t M, int64_t n, int64_t K, int sms) {
@@ -1095,6 +1115,9 @@ int run_swiglu(const LinearArgs& a) {
     st = run_gemv(a, dev);
     if (st != kNoPlan) return st;
   }
+  if (fast_ok && !(a.flags & (QL_FLAG_FORCE_GEMV | QL_FLAG_FORCE_GENERIC | QL_FLAG_FORCE_TCDEC)) &&
+      gemm_ok(a) && ((a.flags & QL_FLAG_FORCE_GEMM) || use_gemm(a.wbits, a.M, a.N, a.K)))
+    return run_gemm(a, dev);   // the tensor-core kernel's SwiGLU epilogue (a.swiglu_n > 0)
   const size_t temp = swiglu_temp_bytes(a.M, n);
   if (!a.ws || a.ws_bytes < temp) return QL_ERR_WORKSPACE;
   LinearArgs b = a;

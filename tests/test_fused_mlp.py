@@ -41,7 +41,7 @@ def _deq(q):
 
 
 @pytest.mark.parametrize("K,N", [(1536, 8960), (4096, 1000), (1536, 256)])
-@pytest.mark.parametrize("M", [1, 4, 8, 16, 64])
+@pytest.mark.parametrize("M", [1, 4, 8, 16, 24, 32, 64, 256])
 @pytest.mark.parametrize("wbits,layout", [(4, 0), (4, 1), (8, 0)])
 def test_gate_up_silu_matches_oracle(K, N, M, wbits, layout):
     bias = (N == 256)
