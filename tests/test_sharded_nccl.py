@@ -187,7 +187,7 @@ def _gather_worker(rank, world, port, result_q):
         result_q.put((rank, False, repr(e)[:300], None))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_gather_back_to_back_flagged(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
