@@ -989,26 +989,29 @@ int run_dec(const LinearArgs& a, DeviceInfo* dev) {
 }
 
 // Where the tensor-core GEMM replaces the decode kernel (measured on B200:
-// forced-path sweeps of both over M = 8..64 on the config-1 to 4 shapes):
-// from 24 batch rows (the decode kernel re-decodes the weights for every
-// 16-row batch chunk); below that where the decode kernel would need a
-// K-split through the workspace — tall-K layers (K >= 3N) from 12 rows
-// (from 8 when K >= 12288), and layers with K >= 4096 wider than 12288
-// (up/gate of 7B-class models, their lm_heads) from 12.  Small layers (at
-// most 4 Mi weights: q/k/v/o of 1.5B-class models) differ: their weights
-// stay in L2 across the batch chunks, so the decode kernel keeps them up
-// to 64 rows from 24 (int8) / 48 (int4) rows — 1536x1536 / 1536x2048 at
-// M 64: int8 6.3 / 6.3 us against 6.9 / 7.3, int4 6.4 / 6.3 against 6.6 /
-// 7.0 — and int4 takes the GEMM from 16 rows (4.1 / 4.3 us against 4.3 /
-// 4.4 at M 16).
+// forced-path sweeps of both over M = 8..64 on the config-1 to 4 shapes and
+// their 8-way column shards).  The decode kernel re-decodes the weights for
+// every 16-row batch chunk, so the GEMM takes every layer from 17 rows —
+// except small layers (at most 4 Mi weights, K < 4096: q/k/v/o of
+// 1.5B-class models), whose weights stay in L2 across the chunks: the decode kernel
+// keeps those up to 64 rows from 17 (int8) / 48 (int4) rows (1536x1536 /
+// 1536x2048 at M 64: int8 6.3 / 6.3 us against the GEMM's 6.9 / 7.3, int4
+// 6.4 / 6.3 against 6.6 / 7.0), while int4 small layers at least 1024 wide
+// take the GEMM from 16 rows (4.1 / 4.3 against 4.3 / 4.4 us).  From 12
+// rows the GEMM also takes K >= 4096 (4096x3584 at M 16: 6.9 against 12.4
+// us; the decode kernel needs a K-split there), tall-K layers (K >= 3N;
+// from 8 rows when K >= 12288) and int4 layers wider than 16384
+// (1536x18992 at M 16: 11.6 against 12.8 us).  Below 12 rows the decode
+// kernel keeps the rest, which also keeps the one-launch greedy head there.
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
-  const bool small = N * K <= (int64_t)1 << 22;
-  if (small && M <= 64 && M >= (wbits == 8 ? 24 : 48)) return false;
+  const bool small = N * K <= (int64_t)1 << 22 && K < 4096;
+  if (small && M <= 64 && M >= (wbits == 8 ? 17 : 48)) return false;
   if (small && wbits == 4 && M >= 16 && N >= 1024) return true;
-  if (M >= 24) return true;
+  if (M > 16) return true;
   if (M < 8) return false;
   if (K >= 3 * N && (M >= 12 || K >= 12288)) return true;
-  return M >= 12 && K >= 4096 && N >= 12288;
+  if (M < 12) return false;
+  return K >= 4096 || (wbits == 4 && N >= 16384);
 }
 
 // Argument checks shared by the linear entry points; out_cols = the
