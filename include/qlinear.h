@@ -226,11 +226,12 @@ int ql_w4a16_quantize(const void* w, int64_t N, int64_t K, int64_t ldw,
  * Replaces the two projections and the activation of the reference's MLP
  * forward, act_fn(gate_proj(x)) * up_proj(x) (HF Qwen2MLP; the reference
  * fuses only the elementwise part, src/kernels/fused_swiglu_triton.py:21-53).
- * The decode kernel applies SwiGLU in its epilogue (fp32, one rounding) and
- * never stores the [M, 2N] product; where the dispatch picks the tensor-core
- * kernel, or the decode kernel has no K-unsplit plan, the product goes
- * through the workspace (size from the *_workspace_size functions; 0 when
- * the fused path runs) and an elementwise kernel. */
+ * The decode kernel and the tensor-core kernel apply SwiGLU in their
+ * epilogues (fp32, one rounding) and never store the [M, 2N] product; only
+ * unaligned operands, a forced portable kernel or a decode kernel without a
+ * K-unsplit plan send the product through the workspace (size from the
+ * *_workspace_size functions; 0 when the decode kernel's fused path runs)
+ * and an elementwise kernel. */
 int ql_w8a16_gate_up_silu(const void* x, int x_dtype,
                           const void* w_q, const void* scale, int scale_dtype,
                           const void* bias, int bias_dtype,

@@ -697,7 +697,19 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
       const int per_sm = o_stages <= 0 ? ctas_per_sm<WBITS, LAYOUT, BN>(g->smem) : 1;
       int sms = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
+      // narrow tiles: one CTA per SM while a single wave of clusters still
+      // covers the tiles, since two CTAs on one SM share its issue slots
+      // for the decode (measured, 12 tiles of 8960->1536: 10 splits 8.1 /
+      // 7.2 us at M 32 / 16 against 14 splits, two CTAs on some SMs, 9.0 /
+      // 8.1 us); otherwise the largest split that fits, two per SM
+      if (per_sm > 1)
+        for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c)
+          if (tiles * c <= (int64_t)(0.95 * sms)) {
+            ks = c;
+            g->clusters_fit = (int)(0.95 * sms) / c;
+            break;
+          }
+      for (int c = ks > 1 ? 1 : std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
         // with two CTAs per SM the query's one-per-SM packing is pessimistic:
         // measured, 70 clusters of 4 of the 32-row tile run as one wave
         int fit = max_active_clusters<WBITS, LAYOUT, BN>(c, g->smem, o_stages <= 0) * per_sm;
