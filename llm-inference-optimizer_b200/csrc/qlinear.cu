@@ -697,19 +697,7 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
       const int per_sm = o_stages <= 0 ? ctas_per_sm<WBITS, LAYOUT, BN>(g->smem) : 1;
       int sms = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      // narrow tiles: one CTA per SM while a single wave of clusters still
-      // covers the tiles, since two CTAs on one SM share its issue slots
-      // for the decode (measured, 12 tiles of 8960->1536: 10 splits 8.1 /
-      // 7.2 us at M 32 / 16 against 14 splits, two CTAs on some SMs, 9.0 /
-      // 8.1 us); otherwise the largest split that fits, two per SM
-      if (per_sm > 1)
-        for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c)
-          if (tiles * c <= (int64_t)(0.95 * sms)) {
-            ks = c;
-            g->clusters_fit = (int)(0.95 * sms) / c;
-            break;
-          }
-      for (int c = ks > 1 ? 1 : std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
+      for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
         // with two CTAs per SM the query's one-per-SM packing is pessimistic:
         // measured, 70 clusters of 4 of the 32-row tile run as one wave
         int fit = max_active_clusters<WBITS, LAYOUT, BN>(c, g->smem, o_stages <= 0) * per_sm;
@@ -717,6 +705,23 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
         if (tiles <= fit) {
           ks = c;
           g->clusters_fit = fit;
+          break;
+        }
+      }
+      // Narrow tiles (two CTAs per SM): two CTAs on one SM share its issue
+      // slots for the decode, so a split that keeps one CTA per SM wins
+      // unless it leaves each CTA more than 1.4x the stages.  Measured on
+      // 12 tiles of 8960->1536 (70 stages) at M 32 / 16: 10 splits of 7
+      // stages 8.0 / 7.1 us against 14 of 5 (two CTAs on some SMs) 9.0 /
+      // 8.1 us; on 28 tiles of 4096->3584 (32 stages): 8 splits of 4
+      // stages 6.9 us against 5 of 7 stages 7.8 us.
+      if (per_sm > 1 && ks > 1) {
+        for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
+          if (tiles * c > (int64_t)(0.95 * sms)) continue;
+          if ((double)cdiv(nk, c) <= 1.4 * (double)cdiv(nk, ks)) {
+            ks = c;
+            g->clusters_fit = (int)(0.95 * sms) / c;
+          }
           break;
         }
       }
@@ -1012,7 +1017,8 @@ int run_dec(const LinearArgs& a, DeviceInfo* dev) {
 // take the GEMM from 16 rows (4.1 / 4.3 against 4.3 / 4.4 us).  From 12
 // rows the GEMM also takes K >= 4096 (4096x3584 at M 16: 6.9 against 12.4
 // us; the decode kernel needs a K-split there), tall-K layers (K >= 3N;
-// from 8 rows when K >= 12288) and int4 layers wider than 16384
+// from 8 rows when K >= 8192: 8960x1536 at M 8, 7.1 against 7.6 us) and
+// int4 layers wider than 16384
 // (1536x18992 at M 16: 11.6 against 12.8 us).  Below 12 rows the decode
 // kernel keeps the rest, which also keeps the one-launch greedy head there.
 bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
@@ -1021,7 +1027,7 @@ bool use_gemm(int wbits, int64_t M, int64_t N, int64_t K) {
   if (small && wbits == 4 && M >= 16 && N >= 1024) return true;
   if (M > 16) return true;
   if (M < 8) return false;
-  if (K >= 3 * N && (M >= 12 || K >= 12288)) return true;
+  if (K >= 3 * N && (M >= 12 || K >= 8192)) return true;
   if (M < 12) return false;
   return K >= 4096 || (wbits == 4 && N >= 16384);
 }
