@@ -1066,6 +1066,16 @@ def run_ours(args):
     e2e_gbs = world * nbytes / (ms_e2e / args.steps * 1e-3) / 1e9
     avg_launch_bytes = nbytes / launches_per_step
     traffic = profiled_traffic("qgemv_w4_config1")
+    # the launch with the largest per-launch time (M 32 down projection)
+    dom_key = max(detail, key=lambda k: detail[k]["us_per_launch"]) if detail else None
+    dominant = None
+    if dom_key:
+        dm, dk, dn = (int(v[1:]) for v in dom_key.split("_"))
+        dbytes = algo_bytes(dm, dk, dn)
+        dus = detail[dom_key]["us_per_launch"]
+        dominant = {"shape": dom_key, "us_per_launch": dus, "bytes_per_launch": dbytes,
+                    "achieved": dbytes / (dus * 1e-6) / 1e9, "frac": dbytes / (dus * 1e-6) / 1e9 / peak,
+                    "traffic": profiled_traffic("qgemm_w4_m32_cluster") if dm == 32 else None}
 
     # free the config-1 weights before the other blocks
     del g_val, g_e2e, layers, ybuf
@@ -1107,10 +1117,11 @@ def run_ours(args):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
                          "frac": per_rank_gbs / peak, "peak_kind": peak_kind,
-                         "kernel": "qgemv_kernel<4,0,*> (M 1, 8) and qgemm_kernel<4,0,32> (M 32): the "
-                                   "step's 216 launches averaged",
+                         "kernel": "qgemv_kernel<4,0,1> (M 1, M 8 gate/up) and qgemm_kernel<4,0,16|32> "
+                                   "(M 8 down, M 32): the step's 216 launches averaged",
                          "bytes_per_launch": avg_launch_bytes,
-                         "traffic": traffic, "pct_of_8TBs": per_rank_gbs / 8000.0},
+                         "traffic": traffic, "pct_of_8TBs": per_rank_gbs / 8000.0,
+                         "dominant_launch": dominant},
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e / args.steps,
