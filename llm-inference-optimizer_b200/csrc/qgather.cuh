@@ -31,8 +31,8 @@
 // units, and CTA c of every rank handles chunk c of every rank's columns:
 //   1. CTA c stores chunk c of this rank's columns into data[e & 1] of every
 //      peer (16-byte stores when the shapes allow), makes them visible
-//      system-wide (fence.sc.sys) and writes ready[rank][c] = e into every
-//      peer's buffer with a system-scope release;
+//      system-wide (one fence.acq_rel.sys) and then writes ready[rank][c] =
+//      e into every peer's buffer (relaxed system-scope stores);
 //   2. it takes the peers in turn: one thread polls its own ready[q][c]
 //      (bounded, acquire) until it has reached e, then the CTA copies chunk
 //      c of q's columns from its own data[e & 1] into `out`.
@@ -100,8 +100,12 @@ struct Params {
   unsigned* err;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// One release fence, then plain (relaxed, system-scope) flag stores: each
+// st.release would wait for the stores before it — the earlier flags to
+// other GPUs included — to be acknowledged over NVLink.
+__device__ __forceinline__ void fence_release_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -312,10 +316,12 @@ __global__ void __launch_bounds__(512) allgather_kernel(const Params p) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();   // the CTA's peer stores, before it publishes them
+    // release: every thread's peer stores (ordered before this thread's by
+    // the barrier) become visible system-wide before any of the flags
+    fence_release_sys();
     for (int k = 1; k < p.world; ++k) {
       const int q = (p.rank + k) % p.world;
-      st_release_sys(reinterpret_cast<unsigned*>(p.peer[q] + L.flags) + p.rank * kMaxCtas + blockIdx.x, e);
+      st_relaxed_sys(reinterpret_cast<unsigned*>(p.peer[q] + L.flags) + p.rank * kMaxCtas + blockIdx.x, e);
     }
     // the epoch advances once every CTA has read it (local bookkeeping only)
     if (atomicAdd(counter, 1u) == gridDim.x - 1) {
