@@ -551,6 +551,7 @@ struct GemmPlan {
   int bn = 0;
   int64_t tiles = 0;
   size_t ws_bytes = 0;   // always 0: K-splits reduce inside their cluster
+  int stage_cap = 0;     // > 0: ring depth at most this (two CTAs per SM)
 };
 
 // Optional override for tuning sweeps: QLINEAR_GEMM_PLAN="ks,stages" (0 =
@@ -575,6 +576,16 @@ GemmPlan plan_gemm(int wbits, int64_t M, int64_t N, int64_t K, int sms) {
   // measured: the 192-row int8 tile pays off from M = 1024 (at 512 its 1.4
   // waves lose to the 128-row tile's 1.9)
   g.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : wbits == 4 ? 256 : M >= 1024 ? 192 : 128;
+  // int8 beyond 128 rows: 128-row activation tiles with a two-stage ring,
+  // so that two CTAs share each SM and one's decode, prologue and epilogue
+  // overlap the other's MMAs (measured, config 3 int8: 12 cases 3.56 ->
+  // 3.13 ms in all; 1536->8960 at M 8192 704 -> 871 TFLOP/s, 14336->4096
+  // 1057 -> 1136; one CTA per SM with the 192/128-row tiles before).  The
+  // int4 tiles lose with it (their 256-row tile feeds the MMAs better).
+  if (wbits == 8 && M > 128) {
+    g.bn = 128;
+    g.stage_cap = 2;
+  }
   g.tiles = cdiv(N, ql::gemm::kTileN) * cdiv(M, g.bn);
   (void)K;
   (void)sms;
@@ -657,13 +668,17 @@ struct GemmLaunch {
 };
 
 template <int WBITS, int LAYOUT, int BN>
-int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
+int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g, int stage_cap = 0) {
   using L = ql::gemm::Layout<WBITS, BN>;
   auto kern = ql::gemm::qgemm_kernel<WBITS, LAYOUT, BN>;
   int S = (int)std::min<size_t>(6, (kSmemOptin - 1024 - 256) / L::kStage);
   int o_ks, o_stages;
   gemm_override(&o_ks, &o_stages);
   if (o_stages > 0) S = std::min(S, o_stages);
+  if (stage_cap > 0) S = std::min(S, stage_cap);
+  // a capped or overridden ring plans its K-split as one CTA per SM and
+  // skips the occupancy cache (kept for the default ring depth)
+  const bool default_ring = o_stages <= 0 && stage_cap <= 0;
   if (S < 3 && BN > 128) return QL_ERR_UNSUPPORTED;
   if (S < 2) return QL_ERR_UNSUPPORTED;
   static std::atomic<unsigned char> done[kMaxDevices];
@@ -694,13 +709,13 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
     if (o_ks > 0) {
       ks = std::min(std::min(o_ks, ql::gemm::kMaxSplits), nk);
     } else {
-      const int per_sm = o_stages <= 0 ? ctas_per_sm<WBITS, LAYOUT, BN>(g->smem) : 1;
+      const int per_sm = default_ring ? ctas_per_sm<WBITS, LAYOUT, BN>(g->smem) : 1;
       int sms = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       for (int c = std::min(ql::gemm::kMaxSplits, nk / 2); c >= 2; --c) {
         // with two CTAs per SM the query's one-per-SM packing is pessimistic:
         // measured, 70 clusters of 4 of the 32-row tile run as one wave
-        int fit = max_active_clusters<WBITS, LAYOUT, BN>(c, g->smem, o_stages <= 0) * per_sm;
+        int fit = max_active_clusters<WBITS, LAYOUT, BN>(c, g->smem, default_ring) * per_sm;
         if (per_sm > 1) fit = std::max(fit, (int)(0.95 * sms * per_sm / c));
         if (tiles <= fit) {
           ks = c;
@@ -740,9 +755,9 @@ int gemm_launch_plan(int64_t tiles, int nk, GemmLaunch* g) {
 
 template <int WBITS, int LAYOUT, int BN>
 int launch_gemm_t(const LinearArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, ql::gemm::Params prm,
-                  int64_t tiles) {
+                  int64_t tiles, int stage_cap) {
   GemmLaunch g;
-  int st = gemm_launch_plan<WBITS, LAYOUT, BN>(tiles, prm.nk, &g);
+  int st = gemm_launch_plan<WBITS, LAYOUT, BN>(tiles, prm.nk, &g, stage_cap);
   if (st != QL_OK) return st;
   if (prm.nh > 0 && ql::gemm::Layout<WBITS, BN>::kPush && g.ks > 1) {
     // SwiGLU mode has no push-mode reduction: the narrow tiles run unsplit
@@ -776,7 +791,7 @@ int gemm_plan_query(int wbits, int layout, int64_t M, int64_t N, int64_t K, int 
   *gp = plan_gemm(wbits, M, N, K, sms);
   const int nk = (int)(K / 128);
   const int bn = gp->bn;
-#define QL_GEMM_PLAN_CASE(W, LY, B) return gemm_launch_plan<W, LY, B>(gp->tiles, nk, gl)
+#define QL_GEMM_PLAN_CASE(W, LY, B) return gemm_launch_plan<W, LY, B>(gp->tiles, nk, gl, gp->stage_cap)
   if (wbits == 8) {
     switch (bn) {
       case 16: QL_GEMM_PLAN_CASE(8, 0, 16);
@@ -840,12 +855,12 @@ int run_gemm_layout(const LinearArgs& a, DeviceInfo* dev, const GemmPlan& g) {
   p.nh = (int)a.swiglu_n;
   p.err = dev->err_word;
   switch (bn) {
-    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.tiles);
-    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.tiles);
-    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.tiles);
-    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.tiles);
-    case 192: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles);
-    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles);
+    case 16: return launch_gemm_t<WBITS, LAYOUT, 16>(a, tx, tw, p, g.tiles, g.stage_cap);
+    case 32: return launch_gemm_t<WBITS, LAYOUT, 32>(a, tx, tw, p, g.tiles, g.stage_cap);
+    case 64: return launch_gemm_t<WBITS, LAYOUT, 64>(a, tx, tw, p, g.tiles, g.stage_cap);
+    case 128: return launch_gemm_t<WBITS, LAYOUT, 128>(a, tx, tw, p, g.tiles, g.stage_cap);
+    case 192: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles, g.stage_cap);
+    default: return launch_gemm_t<WBITS, LAYOUT, WBITS == 4 ? 256 : 192>(a, tx, tw, p, g.tiles, g.stage_cap);
   }
 }
 
