@@ -322,9 +322,10 @@ int ql_linear_argmax_supported(int wbits, int64_t M, int64_t N, int64_t K);
  * block: gate columns, then up columns), then copied into out as well.
  * Outputs of up to 4 MiB are pushed into every peer's gather buffer over
  * NVLink as lines whose 8-byte words carry the call's epoch; larger ones are
- * staged in this rank's own buffer, chunk by chunk, each chunk published by
- * a ready flag (system-scope release), and every peer pulls them over
- * NVLink once the flag has reached the call.  The kernel waits (bounded) for
+ * pushed into the peers' banks chunk by chunk, each chunk published to the
+ * peer by a ready flag (one release fence, then relaxed system-scope flag
+ * stores), and each rank copies a peer's chunk out of its own bank once
+ * that flag has reached the call.  The kernel waits (bounded) for
  * every peer's columns: on completion out holds all N columns on every
  * rank.  All ranks make the same sequence of calls with the same shapes and
  * equally aligned buffers.  Gather buffers: ql_gather_buffer_bytes(max_m, N) bytes, allocated
